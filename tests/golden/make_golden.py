@@ -1,0 +1,88 @@
+"""Regenerate ``tests/golden/reference_fixtures.json`` from the reference project's own fixtures.
+
+Run in a container that has the reference checked out::
+
+    python tests/golden/make_golden.py /path/to/reference
+
+The reference tree does not travel to the GPU box, so the vectors its tests pin are copied
+here once, as data, together with where each came from:
+
+* ``fixtures/gguf/v1/{q8_0,q4_0}.gguf`` + ``manifest.json`` -- the payload bytes of the one
+  32-weight tensor (at ``data_start``), its decoded weights and the ones-vector dot (-8),
+  pinned by QuantizedTests.cs:9-25 and QuantizedAvx2Tests.cs:52-65.
+* ``fixtures/operators/transformer-v1.json`` -- RmsNorm (eps 1e-5), interleaved Rope
+  (head 48, position 37), SwiGlu and 2x48 MHA over 7 tokens, pinned by TransformerOpsTests.cs:8-25.
+* ``fixtures/operators/transformer-v2.json`` -- GQA 4q/2kv x 8 over 3 tokens, half-split RoPE
+  (base 1e6 and a partial rotary case), per-head RmsNorm and bias add, pinned by
+  QwenOperatorTests.cs:28-94.
+* ``fixtures/operators/attention-boundaries-v1.json`` -- 6 heads x 48 over 1, 2, 32, 64 and 128
+  tokens.  Only the expected outputs are stored; the inputs are the deterministic formulas of
+  tools/attention_reference.py:4-6, restated in tests/golden_util.py.
+* The Ternary2 encoding KAT (Ternary2Tests.cs:9-22) and the STQ2 header KAT
+  (MappedTernary2Tests.cs:40-46) are byte strings stated in those tests; they are copied too.
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+OUT = os.path.join(HERE, "reference_fixtures.json")
+
+
+def main(ref: str) -> None:
+    gguf_dir = os.path.join(ref, "fixtures", "gguf", "v1")
+    manifest = json.load(open(os.path.join(gguf_dir, "manifest.json")))
+    gguf = {}
+    for entry in manifest["fixtures"]:
+        if entry["tensor_type_id"] not in (2, 8):
+            continue
+        raw = open(os.path.join(gguf_dir, entry["file"]), "rb").read()
+        start = entry["data_start"] + entry["relative_offset"]
+        payload = raw[start:start + entry["payload_bytes"]]
+        cols, rows = entry["dimensions"]  # GGUF lists the fastest dimension first
+        gguf["q8_0" if entry["tensor_type_id"] == 8 else "q4_0"] = {
+            "source": f"fixtures/gguf/v1/{entry['file']} (sha256 {entry['sha256']})",
+            "rows": rows, "cols": cols, "payload_hex": payload.hex(),
+            "decoded_weights": entry["decoded_weights"], "ones_dot_product": entry["ones_dot_product"],
+        }
+
+    ops = os.path.join(ref, "fixtures", "operators")
+    v1 = json.load(open(os.path.join(ops, "transformer-v1.json")))
+    v2 = json.load(open(os.path.join(ops, "transformer-v2.json")))
+    ab = json.load(open(os.path.join(ops, "attention-boundaries-v1.json")))
+    v1.pop("numpy", None)
+    v2.pop("numpy", None)
+    v1["params"] = {"rms_epsilon": 1e-5, "rope_head_dim": 48, "rope_position": 37,
+                    "attention_head_dim": 48, "attention_tokens": 7,
+                    "stated_in": "tests/Satori.Numerics.Tests/TransformerOpsTests.cs:19-24"}
+
+    out = {
+        "generated_from": "Satori reference fixtures; regenerate with tests/golden/make_golden.py",
+        "tolerance_operator": {"abs": 2e-6, "rel": 2e-6, "stated_in": "QwenOperatorTests.cs:24; TransformerOpsTests.cs:16"},
+        "gguf_v1": gguf,
+        "transformer_v1": v1,
+        "transformer_v2": v2,
+        "attention_boundaries_v1": {"source": "fixtures/operators/attention-boundaries-v1.json",
+                                    "width": 288, "head_dim": 48, "cases": ab["cases"]},
+        "ternary2_encoding_kat": {
+            "source": "tests/Satori.Numerics.Tests/Ternary2Tests.cs:9-22",
+            "weights_nonzero": {"0": 2.0, "1": -2.0}, "rows": 1, "cols": 64, "block_size": 64,
+            "expected_hex": "00008" + "03d09" + "00" * 15,
+        },
+        "stq2_header_kat": {
+            "source": "tests/Satori.Numerics.Tests/MappedTernary2Tests.cs:40-46",
+            "matrix": {"weights": [1.0], "rows": 1, "cols": 1, "block_size": 64},
+            "expected_hex": "53545132" "01002000" "01000000" "01000000"
+                            "40000000" "00000000" "14000000" "00000000",
+        },
+    }
+    with open(OUT, "w") as fh:
+        json.dump(out, fh, separators=(",", ":"))
+        fh.write("\n")
+    print(OUT, os.path.getsize(OUT), "bytes")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
