@@ -1,0 +1,198 @@
+/*
+ * satori_cuda.h -- C ABI of the B200 (sm_100a) decode hot path for Satori.
+ *
+ * Plain C types only: host/device pointers, sizes, ints.  Every function returns a
+ * satori_status; on any error the caller's output buffers are left untouched (the
+ * "commits output only on success" contract of IQuantizedMatrix.Execute,
+ * src/Satori.Core/IQuantizedMatrix.cs:6) and satori_last_error() describes the failure.
+ * Reference paths are relative to the Satori project root.
+ *
+ * Threading: a context serialises its calls on one CUDA stream; handles are not
+ * thread-safe, exactly like DenseSession (src/Satori.Core/Model/DenseSession.cs:11-12).
+ */
+#ifndef SATORI_CUDA_H
+#define SATORI_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SATORI_API __attribute__((visibility("default")))
+#else
+#define SATORI_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum satori_status {
+    SATORI_OK = 0,
+    SATORI_ERR_ARGUMENT = 1,      /* ArgumentException / ArgumentOutOfRangeException */
+    SATORI_ERR_INVALID_DATA = 2,  /* InvalidDataException (non-finite scale, bad STQ2 payload) */
+    SATORI_ERR_NOT_SUPPORTED = 3, /* NotSupportedException (e.g. Q4_0 embedding rows) */
+    SATORI_ERR_CONTEXT_FULL = 4,  /* InvalidOperationException: context limit reached */
+    SATORI_ERR_DISPOSED = 5,      /* ObjectDisposedException */
+    SATORI_ERR_CUDA = 6,          /* device or driver failure (IOException-like fault) */
+    SATORI_ERR_TIMEOUT = 7,       /* a bounded device-side wait expired */
+    SATORI_ERR_OUT_OF_MEMORY = 8
+} satori_status;
+
+/* Weight formats: GGUF Q8_0 / Q4_0 (src/Satori.Core/BlockQuantization.cs:3) and Ternary2 blocks. */
+typedef enum satori_format {
+    SATORI_Q8_0 = 0,
+    SATORI_Q4_0 = 1,
+    SATORI_T2_64 = 64,
+    SATORI_T2_128 = 128,
+    SATORI_T2_256 = 256
+} satori_format;
+
+/* Which reference routine's FP32 operation order a MatVec reproduces (bit for bit). */
+typedef enum satori_order {
+    /* Q8_0/Q4_0: QuantizedMatVec.Execute -> QuantizedAvx2Kernel.Execute (QuantizedMatVec.cs:12-16);
+       Ternary2:  Ternary2MatVec.Execute -> Ternary2Avx2Kernel.Execute (Ternary2MatVec.cs:9-22). */
+    SATORI_ORDER_EXECUTE = 0,
+    /* QuantizedMatVec.ExecuteScalar (:45-78); Ternary2MatVec.ExecuteScalar (Ternary2MatVec.cs:38-42). */
+    SATORI_ORDER_SCALAR = 1,
+    /* QuantizedMatVec.ExecuteBatch -> ExecuteBatchFloat/Dot with FMA (:104-120, 221-365): the decode path. */
+    SATORI_ORDER_BATCH = 2
+} satori_order;
+
+typedef struct satori_ctx satori_ctx;
+typedef struct satori_matrix satori_matrix;
+typedef struct satori_attn satori_attn;
+typedef struct satori_session satori_session;
+
+/* ------------------------------------------------------------------ context */
+/* Opens device `device` (one context per caller; replaces VulkanContext.TryCreate,
+ * src/Satori.Backends.Vulkan/VulkanContext.cs:57). */
+SATORI_API int satori_init(int device, satori_ctx **out);
+SATORI_API int satori_destroy(satori_ctx *ctx);
+/* Copies the calling thread's last error message (NUL-terminated, truncated to n). */
+SATORI_API int satori_last_error(char *buf, size_t n);
+/* Library build identity: writes "satori-b200 <version> sm_100a". */
+SATORI_API int satori_version(char *buf, size_t n);
+/* The context's CUDA stream as an opaque pointer (cudaStream_t), for device-pointer calls. */
+SATORI_API void *satori_stream(satori_ctx *ctx);
+/* Routes the context's device work to a caller-owned cudaStream_t (NULL restores the context's own
+ * stream), e.g. to capture device-pointer calls into the caller's CUDA graph. */
+SATORI_API int satori_set_stream(satori_ctx *ctx, void *stream);
+SATORI_API int satori_synchronize(satori_ctx *ctx);
+
+/* ------------------------------------------------------------------ matrices */
+/* IQuantizedMatrixFactory.Create (src/Satori.Core/IQuantizedMatrixFactory.cs:6) and
+ * Ternary2Matrix.FromPacked (src/Satori.Core/Ternary2Matrix.cs:73-81): validates the payload
+ * exactly like QuantizedMatVec.ValidatePayload (QuantizedMatVec.cs:28-42) /
+ * Ternary2Matrix.ValidatePayload (Ternary2Matrix.cs:83-101), then uploads it once, unchanged in
+ * layout.  `payload` is borrowed only for the duration of the call. */
+SATORI_API int satori_matrix_create(satori_ctx *ctx, const uint8_t *payload, size_t bytes, int rows, int cols,
+                                    int format, satori_matrix **out);
+/* Same, from a payload already in device memory (copied, then validated on the device). */
+SATORI_API int satori_matrix_create_device(satori_ctx *ctx, const uint8_t *device_payload, size_t bytes, int rows,
+                                           int cols, int format, satori_matrix **out);
+/* IQuantizedMatrix.Execute (IQuantizedMatrix.cs:6), GgufQuantizedMatrix.Execute
+ * (src/Satori.Formats.Gguf/GgufQuantizedMatrix.cs:38-40), Ternary2MatVec.Execute /
+ * MappedTernary2Matrix.Execute (Ternary2MatVec.cs:9, MappedTernary2Matrix.cs:43): host x[cols] ->
+ * host y[rows], synchronous, SATORI_ORDER_EXECUTE arithmetic. */
+SATORI_API int satori_matrix_execute(satori_matrix *m, const float *x, float *y);
+/* ExecuteScalar twins (QuantizedMatrix.cs:18-19, GgufQuantizedMatrix.cs:50-52, Ternary2MatVec.cs:38). */
+SATORI_API int satori_matrix_execute_scalar(satori_matrix *m, const float *x, float *y);
+/* QuantizedMatVec.ExecuteBatch / GgufQuantizedMatrix.ExecuteBatch (GgufQuantizedMatrix.cs:43-48):
+ * x[positions][cols] -> y[positions][rows], position-major, host pointers. Q8_0/Q4_0 only. */
+SATORI_API int satori_matrix_execute_batch(satori_matrix *m, const float *x, int positions, float *y);
+/* Device-pointer form of all three on the context stream (asynchronous). */
+SATORI_API int satori_matrix_execute_device(satori_matrix *m, const float *dx, float *dy, int positions, int order);
+/* GgufQuantizedMatrix.ReadRow (GgufQuantizedMatrix.cs:54-61): decodes one row to host memory,
+ * bit-exact; Q4_0 rows are rejected with SATORI_ERR_NOT_SUPPORTED as in the reference.  For
+ * Ternary2 it decodes one row like Ternary2Matrix.Dequantize (Ternary2Matrix.cs:103-120). */
+SATORI_API int satori_matrix_read_row(satori_matrix *m, int row, float *out);
+SATORI_API int satori_matrix_info(const satori_matrix *m, int *rows, int *cols, int *format, size_t *bytes);
+/* Device address of the resident payload (read-only), e.g. for a caller-managed graph. */
+SATORI_API const uint8_t *satori_matrix_device_payload(const satori_matrix *m);
+SATORI_API int satori_matrix_destroy(satori_matrix *m);
+
+/* ------------------------------------------------------------------ quantizers */
+/* Ternary2Matrix.Quantize (Ternary2Matrix.cs:38-71), computed on the device, bit-exact:
+ * host weights[rows*cols] -> host payload (Ternary2 geometry, Ternary2Shape.cs:14). */
+SATORI_API int satori_ternary2_quantize(satori_ctx *ctx, const float *weights, int rows, int cols, int block_size,
+                                        uint8_t *payload);
+/* Not in the reference (it only decodes GGUF): this library's own Q8_0/Q4_0 quantizer, used to
+ * build seeded synthetic weights.  Device pointers, on the context stream. */
+SATORI_API int satori_quantize_q_device(satori_ctx *ctx, const float *d_weights, int rows, int cols, int format,
+                                        uint8_t *d_payload);
+
+/* ------------------------------------------------------------------ attention */
+/* TransformerOps.GroupedAttention (src/Satori.Core/TransformerOps.cs:140-179) on device pointers:
+ * q[q_heads*head_dim], keys/values token-major [tokens][kv_heads*head_dim] -> out[q_heads*head_dim].
+ * Split-K flash decoding (FP32) with partial-softmax merge; asynchronous on the context stream. */
+SATORI_API int satori_grouped_attention_device(satori_ctx *ctx, const float *q, const float *keys,
+                                               const float *values, int q_heads, int kv_heads, int head_dim,
+                                               int tokens, float *out);
+/* Host-pointer twin (synchronous). */
+SATORI_API int satori_grouped_attention(satori_ctx *ctx, const float *q, const float *keys, const float *values,
+                                        int q_heads, int kv_heads, int head_dim, int tokens, float *out);
+/* TransformerOps.RopeHalf (TransformerOps.cs:99-118) on a host vector, in place (FP64 angles). */
+SATORI_API int satori_rope_half(satori_ctx *ctx, float *vector, int n, int head_dim, int position, double base,
+                                int rotary);
+
+/* A device-resident FP32 KV cache for `layers` layers (DenseSession.cs:80-84 layout:
+ * [layer][context][kv_heads*head_dim], token-major). */
+SATORI_API int satori_attn_create(satori_ctx *ctx, int layers, int context, int q_heads, int kv_heads, int head_dim,
+                                  double rope_base, satori_attn **out);
+/* The attention half of DenseForward.Step (DenseForward.cs:135-143): RopeHalf on q and k at
+ * `position`, append k and v at slot `position` of `layer`, GroupedAttention over position+1
+ * tokens.  Host pointers (q/k/v as projected, bias already added); out = context[q_heads*head_dim]. */
+SATORI_API int satori_attn_append(satori_attn *a, int layer, int position, const float *q, const float *k,
+                                  const float *v, float *out);
+SATORI_API int satori_attn_destroy(satori_attn *a);
+
+/* ------------------------------------------------------------------ dense decode session */
+/* One tensor of the model description (names follow GGUF: token_embd.weight, blk.N.attn_q.weight ...). */
+typedef struct satori_tensor {
+    const char *name;
+    const void *data;   /* host or device pointer (unified addressing): payload bytes, or float32 values */
+    size_t bytes;
+    int format;         /* satori_format for matrices, -1 for float32 vectors */
+    int rows, cols;     /* matrices: rows x cols; vectors: rows = length, cols = 1 */
+} satori_tensor;
+
+typedef struct satori_model_desc {
+    int layers, hidden, ffn, q_heads, kv_heads, head_dim, vocab;
+    float rms_epsilon;   /* ModelShape.RmsNormEpsilon cast to float, as DenseForward.cs:49 */
+    double rope_base;
+    int tied_embeddings; /* output projection is token_embd.weight (DenseForward.cs:52) */
+    int n_tensors;
+    const satori_tensor *tensors;
+} satori_model_desc;
+
+/* DenseSession (DenseSession.cs:47-90) with every tensor uploaded once and the whole step
+ * (embed, every layer, final norm, logits, greedy argmax) run on the device. */
+SATORI_API int satori_session_create(satori_ctx *ctx, const satori_model_desc *desc, int context,
+                                     satori_session **out);
+/* Multi-GPU variant: this process is `rank` of `world` (one process per GPU).  Projections are
+ * row-sharded and attention is KV-head sharded; activations are all-gathered over NCCL.
+ * `nccl_unique_id` is the 128-byte ncclUniqueId every rank received from rank 0. */
+SATORI_API int satori_session_create_sharded(satori_ctx *ctx, const satori_model_desc *desc, int context, int rank,
+                                             int world, const void *nccl_unique_id, satori_session **out);
+SATORI_API int satori_nccl_unique_id(void *out128);
+/* DenseSession.Append (DenseSession.cs:111-131) + GreedyTokenSelector.Select
+ * (src/Satori.Core/GreedyTokenSelector.cs:6-16): logits (host, may be NULL) and argmax (may be NULL). */
+SATORI_API int satori_session_append(satori_session *s, int token, float *logits, int *argmax);
+/* Appends `count` tokens one decode step at a time (prefill by repeated decode); writes the last
+ * position's logits/argmax. */
+SATORI_API int satori_session_append_tokens(satori_session *s, const int *tokens, int count, float *logits,
+                                            int *argmax);
+/* Greedy generation: appends `first`, then feeds back the argmax `count - 1` more times; writes the
+ * `count` greedy tokens (TextGenerator.GenerateFromTokens' decode loop, TextGenerator.cs:62-99). */
+SATORI_API int satori_session_generate(satori_session *s, int first, int count, int *tokens_out);
+SATORI_API int satori_session_position(const satori_session *s, int *position);
+SATORI_API int satori_session_reset(satori_session *s);    /* DenseSession.Reset (:189) */
+/* Copies a stage tensor of the last step to the host: 0 = hidden after the last layer,
+ * 1 = final_norm output, 2 = logits (stage parity, ForwardObserver in DenseForward.cs:6). */
+SATORI_API int satori_session_stage(const satori_session *s, int which, float *out, size_t n);
+SATORI_API int satori_session_destroy(satori_session *s);  /* idempotent like DenseSession.Dispose */
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,480 @@
+"""Host-side mirror of Satori's MatVec and attention API over the CUDA C ABI.
+
+Names, argument meaning and error behaviour follow the C# reference so that a caller (or a
+test) reads the same:
+
+* ``QuantizedMatrixShape`` / ``BlockQuantization``     -- src/Satori.Core/QuantizedMatrixShape.cs:5-22
+* ``CudaMatrixFactory.create``                         -- IQuantizedMatrixFactory.Create (IQuantizedMatrixFactory.cs:6)
+* ``CudaQuantizedMatrix.execute``                      -- IQuantizedMatrix.Execute (IQuantizedMatrix.cs:6)
+* ``Ternary2Matrix`` / ``Ternary2MatVec``              -- src/Satori.Core/Ternary2Matrix.cs, Ternary2MatVec.cs
+* ``MappedTernary2Matrix``                             -- src/Satori.Core/MappedTernary2Matrix.cs
+* ``TransformerOps.grouped_attention`` / ``rope_half`` -- src/Satori.Core/TransformerOps.cs:99-179
+
+All arithmetic runs on the GPU through ``libsatori_cuda.so``; this module only moves bytes.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+import os
+import struct
+import threading
+
+import numpy as np
+
+from . import _lib
+from ._lib import ArgumentError, DisposedError, InvalidDataError, check
+
+_vp = C.c_void_p
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def _f32(a, n: int | None = None, name: str = "vector") -> np.ndarray:
+    v = np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+    if n is not None and v.size != n:
+        raise ArgumentError(_lib.ERR_ARGUMENT, f"{name} length {v.size} does not match {n}")
+    return v
+
+
+def _u8(a) -> np.ndarray:
+    if isinstance(a, (bytes, bytearray, memoryview)):
+        return np.frombuffer(bytes(a), dtype=np.uint8)
+    return np.ascontiguousarray(a, dtype=np.uint8).reshape(-1)
+
+
+def _commit(y: np.ndarray, output):
+    """Output is written only after the device call succeeded (IQuantizedMatrix.cs:6)."""
+    if output is None:
+        return y
+    if output.dtype != np.float32 or output.size != y.size:
+        raise ArgumentError(_lib.ERR_ARGUMENT, "output length does not match")
+    output.reshape(-1)[:] = y
+    return output
+
+
+# --------------------------------------------------------------------------- context
+class Context:
+    """One CUDA device and stream (one per caller thread, like VulkanContext)."""
+
+    def __init__(self, device: int = 0):
+        h = _vp()
+        check(_lib.lib().satori_init(device, C.byref(h)), "satori_init")
+        self._h = h
+        self.device = device
+
+    @property
+    def handle(self):
+        if not self._h:
+            raise DisposedError(_lib.ERR_DISPOSED, "context is disposed")
+        return self._h
+
+    @property
+    def stream(self) -> int:
+        return _lib.lib().satori_stream(self.handle) or 0
+
+    def set_stream(self, stream_ptr: int | None) -> None:
+        """Route device work to a caller-owned cudaStream_t (None restores the context's own)."""
+        check(_lib.lib().satori_set_stream(self.handle, stream_ptr), "set_stream")
+
+    def synchronize(self) -> None:
+        check(_lib.lib().satori_synchronize(self.handle), "satori_synchronize")
+
+    def close(self) -> None:
+        if self._h:
+            _lib.lib().satori_destroy(self._h)
+            self._h = _vp()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+_default_contexts: dict[int, Context] = {}
+_default_lock = threading.Lock()
+
+
+def default_context(device: int = 0) -> Context:
+    with _default_lock:
+        ctx = _default_contexts.get(device)
+        if ctx is None:
+            ctx = _default_contexts[device] = Context(device)
+        return ctx
+
+
+# --------------------------------------------------------------------------- shapes
+class BlockQuantization(enum.IntEnum):
+    """src/Satori.Core/BlockQuantization.cs:3 (the two formats on this path)."""
+    Q8_0 = _lib.Q8_0
+    Q4_0 = _lib.Q4_0
+
+
+class QuantizedMatrixShape:
+    """QuantizedMatrixShape (QuantizedMatrixShape.cs:5-22): positive dims, complete 32-weight rows."""
+
+    def __init__(self, rows: int, columns: int, fmt: BlockQuantization):
+        fmt = BlockQuantization(fmt)
+        self.block_elements, self.block_bytes = (32, 34) if fmt == BlockQuantization.Q8_0 else (32, 18)
+        if rows <= 0 or columns <= 0 or columns % self.block_elements != 0:
+            raise ArgumentError(_lib.ERR_ARGUMENT,
+                                f"Positive dimensions and complete {self.block_elements}-weight rows required.")
+        self.rows, self.columns, self.format = rows, columns, fmt
+        self.byte_length = rows * (columns // self.block_elements) * self.block_bytes
+        if self.byte_length > 0x7FFFFFFF:
+            raise ArgumentError(_lib.ERR_ARGUMENT, "payload exceeds Int32 limits")
+
+    def __repr__(self):
+        return f"QuantizedMatrixShape({self.rows}, {self.columns}, {self.format.name})"
+
+
+def ternary2_byte_length(rows: int, columns: int, block_size: int) -> int:
+    """Ternary2Shape.ByteLength (Ternary2Shape.cs:14)."""
+    if rows <= 0 or columns <= 0:
+        raise ArgumentError(_lib.ERR_ARGUMENT, "dimensions must be positive")
+    if block_size not in (64, 128, 256):
+        raise ArgumentError(_lib.ERR_ARGUMENT, "Supported block sizes: 64, 128, 256.")
+    n = rows * ((columns + block_size - 1) // block_size) * (4 + block_size // 4)
+    if n > 0x7FFFFFFF:
+        raise ArgumentError(_lib.ERR_ARGUMENT, "payload exceeds Int32 limits")
+    return n
+
+
+# --------------------------------------------------------------------------- resident matrices
+class CudaQuantizedMatrix:
+    """A resident payload on the device (IQuantizedMatrix).  Q8_0/Q4_0 or Ternary2."""
+
+    def __init__(self, ctx: Context, payload, rows: int, columns: int, fmt: int):
+        self.ctx = ctx
+        h = _vp()
+        data = _u8(payload)
+        check(_lib.lib().satori_matrix_create(ctx.handle, _ptr(data), data.size, rows, columns, fmt, C.byref(h)),
+              "create")
+        self._h = h
+        self.rows, self.columns, self.format = rows, columns, fmt
+
+    @classmethod
+    def from_device(cls, ctx: Context, device_ptr: int, nbytes: int, rows: int, columns: int, fmt: int):
+        m = cls.__new__(cls)
+        m.ctx = ctx
+        h = _vp()
+        check(_lib.lib().satori_matrix_create_device(ctx.handle, device_ptr, nbytes, rows, columns, fmt, C.byref(h)),
+              "create_device")
+        m._h = h
+        m.rows, m.columns, m.format = rows, columns, fmt
+        return m
+
+    @property
+    def handle(self):
+        if not self._h:
+            raise DisposedError(_lib.ERR_DISPOSED, "matrix is disposed")
+        return self._h
+
+    def execute(self, input, output: np.ndarray | None = None) -> np.ndarray:
+        """IQuantizedMatrix.Execute: output is written only when the call succeeds."""
+        x = _f32(input, self.columns, "input")
+        y = np.empty(self.rows, np.float32)
+        check(_lib.lib().satori_matrix_execute(self.handle, _ptr(x), _ptr(y)), "execute")
+        return _commit(y, output)
+
+    def execute_scalar(self, input, output: np.ndarray | None = None) -> np.ndarray:
+        x = _f32(input, self.columns, "input")
+        y = np.empty(self.rows, np.float32)
+        check(_lib.lib().satori_matrix_execute_scalar(self.handle, _ptr(x), _ptr(y)), "execute_scalar")
+        return _commit(y, output)
+
+    def execute_batch(self, input, positions: int, output: np.ndarray | None = None, threads: int = 1) -> np.ndarray:
+        """QuantizedMatVec.ExecuteBatch (position-major); `threads` is accepted for signature parity."""
+        if positions <= 0 or threads <= 0:
+            raise ArgumentError(_lib.ERR_ARGUMENT, "positions and threads must be positive")
+        x = _f32(input, positions * self.columns, "input")
+        y = np.empty(positions * self.rows, np.float32)
+        check(_lib.lib().satori_matrix_execute_batch(self.handle, _ptr(x), positions, _ptr(y)), "execute_batch")
+        return _commit(y, output)
+
+    def execute_device(self, dx: int, dy: int, positions: int = 1, order: int = _lib.ORDER_BATCH) -> None:
+        check(_lib.lib().satori_matrix_execute_device(self.handle, dx, dy, positions, order), "execute_device")
+
+    def read_row(self, row: int) -> np.ndarray:
+        """GgufQuantizedMatrix.ReadRow (bit-exact decode; Q4_0 rejected as in the reference)."""
+        out = np.empty(self.columns, np.float32)
+        check(_lib.lib().satori_matrix_read_row(self.handle, row, _ptr(out)), "read_row")
+        return out
+
+    @property
+    def device_payload(self) -> int:
+        return _lib.lib().satori_matrix_device_payload(self.handle) or 0
+
+    def dispose(self) -> None:
+        if self._h:
+            _lib.lib().satori_matrix_destroy(self._h)
+            self._h = _vp()
+
+    close = dispose
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.dispose()
+
+    def __del__(self):
+        try:
+            self.dispose()
+        except Exception:
+            pass
+
+
+class CudaMatrixFactory:
+    """IQuantizedMatrixFactory over the GPU (the seam VulkanContext implements in the reference)."""
+
+    def __init__(self, ctx: Context | None = None):
+        self.ctx = ctx or default_context()
+
+    def create(self, payload, shape: QuantizedMatrixShape) -> CudaQuantizedMatrix:
+        data = _u8(payload)
+        if data.size != shape.byte_length:
+            raise ArgumentError(_lib.ERR_ARGUMENT, "Incorrect quantized payload length.")
+        return CudaQuantizedMatrix(self.ctx, data, shape.rows, shape.columns, int(shape.format))
+
+
+# --------------------------------------------------------------------------- Ternary2
+_STQ2_HEADER = 32
+
+
+class Ternary2Matrix:
+    """Validated row-major ternary weights with FP32 block scales (Ternary2Matrix.cs)."""
+
+    def __init__(self, rows: int, columns: int, block_size: int, data: np.ndarray, ctx: Context | None = None,
+                 _validated_device: CudaQuantizedMatrix | None = None):
+        self.rows, self.columns, self.block_size = rows, columns, block_size
+        self._data = data
+        self._ctx = ctx or default_context()
+        self._dev = _validated_device
+
+    @property
+    def byte_length(self) -> int:
+        return self._data.size
+
+    @property
+    def data(self) -> np.ndarray:
+        return self._data
+
+    def copy_data_to(self, destination: np.ndarray) -> None:
+        destination.reshape(-1)[: self._data.size] = self._data
+
+    @property
+    def device(self) -> CudaQuantizedMatrix:
+        if self._dev is None:
+            self._dev = CudaQuantizedMatrix(self._ctx, self._data, self.rows, self.columns, self.block_size)
+        return self._dev
+
+    @staticmethod
+    def quantize(weights, rows: int, columns: int, block_size: int = 64, ctx: Context | None = None) -> "Ternary2Matrix":
+        """Ternary2Matrix.Quantize (Ternary2Matrix.cs:38-71), computed on the device, bit-exact."""
+        ctx = ctx or default_context()
+        n = ternary2_byte_length(rows, columns, block_size)
+        w = np.ascontiguousarray(weights, dtype=np.float32).reshape(-1)
+        if w.size != rows * columns:
+            raise ArgumentError(_lib.ERR_ARGUMENT, "Weights must match matrix dimensions.")
+        out = np.zeros(n, np.uint8)
+        check(_lib.lib().satori_ternary2_quantize(ctx.handle, _ptr(w), rows, columns, block_size, _ptr(out)), "quantize")
+        return Ternary2Matrix(rows, columns, block_size, out, ctx)
+
+    @staticmethod
+    def from_packed(rows: int, columns: int, block_size: int, data, ctx: Context | None = None) -> "Ternary2Matrix":
+        """Ternary2Matrix.FromPacked (:73-81): length and payload validated (ArgumentError)."""
+        ctx = ctx or default_context()
+        owned = _u8(data).copy()
+        if owned.size != ternary2_byte_length(rows, columns, block_size):
+            raise ArgumentError(_lib.ERR_ARGUMENT, "Payload length must match matrix dimensions.")
+        dev = CudaQuantizedMatrix(ctx, owned, rows, columns, block_size)
+        return Ternary2Matrix(rows, columns, block_size, owned, ctx, dev)
+
+    def dequantize(self, destination: np.ndarray | None = None) -> np.ndarray:
+        """Ternary2Matrix.Dequantize (:103-120), decoded on the device row by row."""
+        out = np.empty((self.rows, self.columns), np.float32)
+        for r in range(self.rows):
+            out[r] = self.device.read_row(r)
+        return _commit(out.reshape(-1), destination)
+
+    def save(self, path: str) -> None:
+        """Ternary2Matrix.Save (:29-36): STQ2 header then the payload; refuses to overwrite."""
+        with open(path, "xb") as fh:
+            fh.write(stq2_header(self.rows, self.columns, self.block_size))
+            fh.write(self._data.tobytes())
+
+
+def stq2_header(rows: int, columns: int, block_size: int) -> bytes:
+    """Ternary2FileFormat.WriteHeader (Ternary2FileFormat.cs:9-19)."""
+    n = ternary2_byte_length(rows, columns, block_size)
+    return b"STQ2" + struct.pack("<HHiiiiq", 1, _STQ2_HEADER, rows, columns, block_size, 0, n)
+
+
+def stq2_read_header(header: bytes) -> tuple[int, int, int]:
+    """Ternary2FileFormat.ReadHeader (Ternary2FileFormat.cs:21-35); InvalidDataError on any mismatch."""
+    if len(header) < _STQ2_HEADER or header[:4] != b"STQ2":
+        raise InvalidDataError(_lib.ERR_INVALID_DATA, "Unsupported Ternary2 header.")
+    version, size, rows, cols, bs, pad, length = struct.unpack("<HHiiiiq", header[4:32])
+    if version != 1 or size != _STQ2_HEADER or pad != 0:
+        raise InvalidDataError(_lib.ERR_INVALID_DATA, "Unsupported Ternary2 header.")
+    try:
+        want = ternary2_byte_length(rows, cols, bs)
+    except ArgumentError as e:
+        raise InvalidDataError(_lib.ERR_INVALID_DATA, "Invalid Ternary2 shape or payload.") from e
+    if length != want:
+        raise InvalidDataError(_lib.ERR_INVALID_DATA, "Payload length disagrees with matrix shape.")
+    return rows, cols, bs
+
+
+def _check_t2_vectors(rows, cols, input, output):
+    """Ternary2MatVec.ValidateVectors (Ternary2MatVec.cs:30-36)."""
+    n_in = np.asarray(input).size
+    n_out = rows if output is None else np.asarray(output).size
+    if n_in != cols or n_out != rows:
+        raise ArgumentError(_lib.ERR_ARGUMENT, "Vector lengths must match matrix dimensions.")
+    if output is not None and isinstance(input, np.ndarray) and np.shares_memory(input, output):
+        raise ArgumentError(_lib.ERR_ARGUMENT, "Output must not overlap input.")
+
+
+class Ternary2MatVec:
+    """Ternary2MatVec (Ternary2MatVec.cs:7-50): Execute runs the AVX2-order arithmetic on the GPU."""
+
+    @staticmethod
+    def execute(matrix: Ternary2Matrix, input, output: np.ndarray | None = None) -> np.ndarray:
+        _check_t2_vectors(matrix.rows, matrix.columns, input, output)
+        return matrix.device.execute(input, output)
+
+    execute_avx2 = execute
+
+    @staticmethod
+    def execute_scalar(matrix: Ternary2Matrix, input, output: np.ndarray | None = None) -> np.ndarray:
+        _check_t2_vectors(matrix.rows, matrix.columns, input, output)
+        return matrix.device.execute_scalar(input, output)
+
+
+class MappedTernary2Matrix:
+    """A validated STQ2 file executed on the GPU (MappedTernary2Matrix.cs:9-55).
+
+    The payload is read once from the mapped file and uploaded unchanged; every invalid header,
+    length or payload raises InvalidDataError, as the reference's constructor does (:25-28).
+    """
+
+    def __init__(self, path: str, ctx: Context | None = None):
+        ctx = ctx or default_context()
+        size = os.path.getsize(path)
+        mm = np.memmap(path, dtype=np.uint8, mode="r") if size else np.zeros(0, np.uint8)
+        if mm.size < _STQ2_HEADER:
+            raise InvalidDataError(_lib.ERR_INVALID_DATA, "Truncated Ternary2 header.")
+        rows, cols, bs = stq2_read_header(bytes(mm[:_STQ2_HEADER]))
+        n = ternary2_byte_length(rows, cols, bs)
+        if mm.size != _STQ2_HEADER + n:
+            raise InvalidDataError(_lib.ERR_INVALID_DATA, "Truncated payload or trailing file data.")
+        try:
+            self._dev = CudaQuantizedMatrix(ctx, np.ascontiguousarray(mm[_STQ2_HEADER:]), rows, cols, bs)
+        except ArgumentError as e:
+            raise InvalidDataError(_lib.ERR_INVALID_DATA, "Invalid Ternary2 shape or payload.") from e
+        del mm
+        self.rows, self.columns, self.block_size, self.byte_length = rows, cols, bs, n
+        self._disposed = False
+
+    def _live(self) -> CudaQuantizedMatrix:
+        if self._disposed:
+            raise DisposedError(_lib.ERR_DISPOSED, "Cannot access a disposed object.")
+        return self._dev
+
+    def execute(self, input, output: np.ndarray | None = None) -> np.ndarray:
+        dev = self._live()
+        _check_t2_vectors(self.rows, self.columns, input, output)
+        return dev.execute(input, output)
+
+    def execute_scalar(self, input, output: np.ndarray | None = None) -> np.ndarray:
+        dev = self._live()
+        _check_t2_vectors(self.rows, self.columns, input, output)
+        return dev.execute_scalar(input, output)
+
+    def dispose(self) -> None:
+        if not self._disposed:
+            self._dev.dispose()
+            self._disposed = True
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.dispose()
+
+
+# --------------------------------------------------------------------------- attention
+class TransformerOps:
+    """GPU restatements of the attention operators (TransformerOps.cs)."""
+
+    @staticmethod
+    def grouped_attention(query, keys, values, query_heads: int, kv_heads: int, head_dimension: int,
+                          token_count: int, output: np.ndarray | None = None, ctx: Context | None = None) -> np.ndarray:
+        """TransformerOps.GroupedAttention (:140-179)."""
+        ctx = ctx or default_context()
+        if head_dimension <= 0 or query_heads <= 0 or kv_heads <= 0 or query_heads % kv_heads or token_count <= 0:
+            raise ArgumentError(_lib.ERR_ARGUMENT, "Invalid grouped-attention dimensions.")
+        q = _f32(query, query_heads * head_dimension, "query")
+        k = _f32(keys, token_count * kv_heads * head_dimension, "keys")
+        v = _f32(values, token_count * kv_heads * head_dimension, "values")
+        out = np.empty(q.size, np.float32)
+        check(_lib.lib().satori_grouped_attention(ctx.handle, _ptr(q), _ptr(k), _ptr(v), query_heads, kv_heads,
+                                                  head_dimension, token_count, _ptr(out)), "grouped_attention")
+        return _commit(out, output)
+
+    @staticmethod
+    def attention(query, keys, values, head_dimension: int, token_count: int, output=None, ctx=None) -> np.ndarray:
+        """TransformerOps.Attention (:62-94): equal query and KV heads."""
+        q = _f32(query)
+        if head_dimension <= 0 or q.size == 0 or q.size % head_dimension:
+            raise ArgumentError(_lib.ERR_ARGUMENT, "Invalid attention dimensions.")
+        heads = q.size // head_dimension
+        return TransformerOps.grouped_attention(q, keys, values, heads, heads, head_dimension, token_count, output, ctx)
+
+    @staticmethod
+    def rope_half(vector: np.ndarray, head_dimension: int, position: int, frequency_base: float,
+                  rotary_dimensions: int, ctx: Context | None = None) -> np.ndarray:
+        """TransformerOps.RopeHalf (:99-118), in place on a float32 array."""
+        ctx = ctx or default_context()
+        if vector.dtype != np.float32 or not vector.flags.c_contiguous:
+            raise ArgumentError(_lib.ERR_ARGUMENT, "vector must be a contiguous float32 array")
+        check(_lib.lib().satori_rope_half(ctx.handle, _ptr(vector), vector.size, head_dimension, position,
+                                          float(frequency_base), rotary_dimensions), "rope_half")
+        return vector
+
+
+class AttentionCache:
+    """Device KV cache plus the attention half of DenseForward.Step (DenseForward.cs:135-143)."""
+
+    def __init__(self, layers: int, context: int, q_heads: int, kv_heads: int, head_dim: int, rope_base: float,
+                 ctx: Context | None = None):
+        self.ctx = ctx or default_context()
+        h = _vp()
+        check(_lib.lib().satori_attn_create(self.ctx.handle, layers, context, q_heads, kv_heads, head_dim,
+                                            float(rope_base), C.byref(h)), "attn_create")
+        self._h = h
+        self.q_width, self.kv_width = q_heads * head_dim, kv_heads * head_dim
+
+    def append(self, layer: int, position: int, q, k, v) -> np.ndarray:
+        if not self._h:
+            raise DisposedError(_lib.ERR_DISPOSED, "attention cache is disposed")
+        qv, kv, vv = _f32(q, self.q_width, "q"), _f32(k, self.kv_width, "k"), _f32(v, self.kv_width, "v")
+        out = np.empty(self.q_width, np.float32)
+        check(_lib.lib().satori_attn_append(self._h, layer, position, _ptr(qv), _ptr(kv), _ptr(vv), _ptr(out)), "append")
+        return out
+
+    def dispose(self):
+        if self._h:
+            _lib.lib().satori_attn_destroy(self._h)
+            self._h = _vp()
+
+    def __del__(self):
+        try:
+            self.dispose()
+        except Exception:
+            pass

@@ -1,0 +1,494 @@
+// attention.cu -- decode grouped-query attention for sm_100a.
+//
+// Restates TransformerOps.GroupedAttention (src/Satori.Core/TransformerOps.cs:140-179): query
+// head h attends to KV head h / (q_heads / kv_heads) over the causal prefix; softmax of
+// (q . k) / sqrt(head_dim), weighted sum of v.  The reference works in FP64; this kernel works in
+// FP32 with split-K flash decoding, which stays within the stated 1e-5 relative + 1e-6 absolute
+// of the FP64 result for finite scores.  Where FP32 scores overflow (|q . k| beyond FP32 range --
+// the reference's own FLT_MAX test), the merge kernel recomputes that head in FP64 on the device.
+//
+// Work decomposition: one CTA per (sequence split, KV head, group of up to 8 query heads).  The
+// CTA's four warps walk 32-token blocks of the split; each lane owns 4 contiguous dims of the
+// 128-wide head, so a token's K or V row is one coalesced 512-byte warp load and every K/V byte
+// is read from HBM once for all query heads of its group.  Per token the 8 head partial dots are
+// reduced across the warp with a transposed butterfly (9 shuffles instead of 40).  Online softmax
+// state (m, l, acc) is kept per warp, merged per CTA into one partial record, and the records of
+// all splits are merged by a second kernel.
+#include "attention.cuh"
+#include "common.cuh"
+
+#include <algorithm>
+#include <cmath>
+
+namespace satori {
+
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kTokBlock = 32;
+
+struct AttnParams {
+    const float *q, *keys, *values;
+    int q_heads, kv_heads, head_dim, group, ngroups;
+    int tokens;
+    const int *tokens_dev;
+    int nsplit;
+    float scale;
+    float *scratch;
+    float *out;
+    int use_pdl;
+};
+
+// Sum across the warp of N values per lane, N a power of two <= 8.  On return v[0] holds, in
+// every lane, the total of head (lane / (32 / N)); all lanes of a head hold identical bits.
+template <int N>
+__device__ __forceinline__ float transpose_reduce(float (&v)[8], int lane)
+{
+    int off = 16;
+#pragma unroll
+    for (int n = N; n > 1; n >>= 1, off >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float send = upper ? v[i] : v[i + n / 2];
+            const float keep = upper ? v[i + n / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, off);
+        }
+    }
+#pragma unroll
+    for (; off >= 1; off >>= 1) v[0] = v[0] + __shfl_xor_sync(0xFFFFFFFFu, v[0], off);
+    return v[0];
+}
+
+template <int DPL, bool VEC4>
+__device__ __forceinline__ void load_row(const float *row, int lane, int hd, float (&r)[DPL])
+{
+    if (VEC4) {
+        const float4 t = __ldg(reinterpret_cast<const float4 *>(row) + lane);
+        r[0] = t.x; r[1] = t.y; r[2] = t.z; r[3] = t.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+            const int d = lane + 32 * i;
+            r[i] = d < hd ? __ldg(row + d) : 0.0f;
+        }
+    }
+}
+
+template <int DPL, bool VEC4>
+__device__ __forceinline__ int dim_of(int lane, int i) { return VEC4 ? 4 * lane + i : lane + 32 * i; }
+
+template <int DPL, bool VEC4, int GMAX>
+__global__ void __launch_bounds__(kWarps * 32) attn_partial_kernel(AttnParams p)
+{
+    constexpr int R = 32 / GMAX;  // lanes per head after the transposed reduction
+    __shared__ float P[kWarps][GMAX][kTokBlock];
+    __shared__ float wm[kWarps][GMAX], wl[kWarps][GMAX];
+    __shared__ float wacc[kWarps][GMAX][DPL * 32];
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int split = blockIdx.x;
+    const int kvh = blockIdx.y / p.ngroups, grp = blockIdx.y % p.ngroups;
+    const int h0 = kvh * p.group + grp * GMAX;
+    const int gc = min(GMAX, p.group - grp * GMAX);
+    const int hd = p.head_dim;
+    const int kvw = p.kv_heads * hd;
+    const int hl = lane / R;
+
+    if (p.use_pdl) pdl_wait();
+    const int T = p.tokens_dev ? *p.tokens_dev : p.tokens;
+    const int t0 = (int)(((long long)T * split) / p.nsplit);
+    const int t1 = (int)(((long long)T * (split + 1)) / p.nsplit);
+
+    float qr[GMAX][DPL];
+#pragma unroll
+    for (int h = 0; h < GMAX; ++h)
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+            const int d = dim_of<DPL, VEC4>(lane, i);
+            qr[h][i] = (h < gc && d < hd) ? p.q[(h0 + h) * hd + d] : 0.0f;
+        }
+    float acc[GMAX][DPL];
+#pragma unroll
+    for (int h = 0; h < GMAX; ++h)
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[h][i] = 0.0f;
+    float m_my = -INFINITY, l_my = 0.0f;
+
+    const float *kbase = p.keys + (long long)kvh * hd;
+    const float *vbase = p.values + (long long)kvh * hd;
+
+    for (int tb = t0 + warp * kTokBlock; tb < t1; tb += kWarps * kTokBlock) {
+        const int nt = min(kTokBlock, t1 - tb);
+        float sc[kTokBlock];
+#pragma unroll
+        for (int j = 0; j < kTokBlock; ++j) {
+            if (j < nt) {
+                float kr[DPL];
+                load_row<DPL, VEC4>(kbase + (long long)(tb + j) * kvw, lane, hd, kr);
+                float v[8];
+#pragma unroll
+                for (int h = 0; h < 8; ++h) v[h] = 0.0f;
+#pragma unroll
+                for (int h = 0; h < GMAX; ++h) {
+                    float s = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < DPL; ++i) s = fmaf(qr[h][i], kr[i], s);
+                    v[h] = s;
+                }
+                sc[j] = transpose_reduce<GMAX>(v, lane) * p.scale;
+            } else {
+                sc[j] = -INFINITY;
+            }
+        }
+        float mb = sc[0];
+#pragma unroll
+        for (int j = 1; j < kTokBlock; ++j) mb = fmaxf(mb, sc[j]);
+        const float m_new = fmaxf(m_my, mb);
+        const float alpha = m_my == -INFINITY ? 0.0f : expf(m_my - m_new);
+        float lsum = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kTokBlock; ++j) {
+            const float pj = j < nt ? expf(sc[j] - m_new) : 0.0f;
+            lsum += pj;
+            if ((j % R) == (lane % R)) P[warp][hl][j] = pj;
+        }
+        l_my = l_my * alpha + lsum;
+        m_my = m_new;
+        float alpha_h[GMAX];
+#pragma unroll
+        for (int h = 0; h < GMAX; ++h) alpha_h[h] = __shfl_sync(0xFFFFFFFFu, alpha, h * R);
+#pragma unroll
+        for (int h = 0; h < GMAX; ++h)
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) acc[h][i] *= alpha_h[h];
+        __syncwarp();
+        for (int j = 0; j < nt; ++j) {
+            float vr[DPL];
+            load_row<DPL, VEC4>(vbase + (long long)(tb + j) * kvw, lane, hd, vr);
+#pragma unroll
+            for (int h = 0; h < GMAX; ++h) {
+                const float pj = P[warp][h][j];
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) acc[h][i] = fmaf(pj, vr[i], acc[h][i]);
+            }
+        }
+        __syncwarp();
+    }
+
+    // Per-warp state -> shared memory, then one merged record per (split, head).
+    if (lane % R == 0) {
+        wm[warp][hl] = m_my;
+        wl[warp][hl] = l_my;
+    }
+#pragma unroll
+    for (int h = 0; h < GMAX; ++h)
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) wacc[warp][h][i * 32 + lane] = acc[h][i];
+    __syncthreads();
+
+    const int rec_stride = hd + 2;
+    for (int idx = threadIdx.x; idx < gc * (hd + 2); idx += blockDim.x) {
+        const int h = idx / (hd + 2), e = idx - h * (hd + 2);
+        float m = wm[0][h];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) m = fmaxf(m, wm[w][h]);
+        float val = 0.0f;
+        if (e == 0) {
+            val = m;
+        } else {
+            for (int w = 0; w < kWarps; ++w) {
+                const float f = wm[w][h] == -INFINITY ? 0.0f : expf(wm[w][h] - m);
+                float x;
+                if (e == 1) {
+                    x = wl[w][h];
+                } else {
+                    const int d = e - 2;
+                    int lane_d, i_d;
+                    if (VEC4) { lane_d = d >> 2; i_d = d & 3; } else { lane_d = d & 31; i_d = d >> 5; }
+                    x = wacc[w][h][i_d * 32 + lane_d];
+                }
+                val = fmaf(x, f, val);
+            }
+        }
+        p.scratch[((long long)split * p.q_heads + h0 + h) * rec_stride + e] = val;
+    }
+    if (p.use_pdl) pdl_launch_dependents();
+}
+
+// FP64 recompute of one head (the reference's arithmetic), used when FP32 scores overflowed.
+__device__ void head_fp64(const AttnParams &p, int head, int T, double *sbuf, float *out)
+{
+    const int hd = p.head_dim, kvw = p.kv_heads * hd;
+    const int kvh = head / p.group;
+    const float *q = p.q + (long long)head * hd;
+    const double scale = 1.0 / sqrt((double)hd);
+    __shared__ double red[128];
+    // pass 1: max score
+    double mx = -INFINITY;
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const float *k = p.keys + (long long)t * kvw + kvh * hd;
+        double dot = 0;
+        for (int j = 0; j < hd; ++j) dot = __dadd_rn(dot, __dmul_rn((double)q[j], (double)k[j]));
+        mx = fmax(mx, __dmul_rn(dot, scale));
+    }
+    red[threadIdx.x] = mx;
+    __syncthreads();
+    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+        if (threadIdx.x < s) red[threadIdx.x] = fmax(red[threadIdx.x], red[threadIdx.x + s]);
+        __syncthreads();
+    }
+    mx = red[0];
+    __syncthreads();
+    // pass 2: total
+    double tot = 0;
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const float *k = p.keys + (long long)t * kvw + kvh * hd;
+        double dot = 0;
+        for (int j = 0; j < hd; ++j) dot = __dadd_rn(dot, __dmul_rn((double)q[j], (double)k[j]));
+        tot = __dadd_rn(tot, exp(__dsub_rn(__dmul_rn(dot, scale), mx)));
+    }
+    red[threadIdx.x] = tot;
+    __syncthreads();
+    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+        if (threadIdx.x < s) red[threadIdx.x] = __dadd_rn(red[threadIdx.x], red[threadIdx.x + s]);
+        __syncthreads();
+    }
+    tot = red[0];
+    __syncthreads();
+    // pass 3: sum_t (p_t / total) * v_t, in token order per dim
+    double sum[2] = {0, 0};
+    for (int tc = 0; tc < T; tc += blockDim.x) {
+        const int t = tc + threadIdx.x;
+        if (t < T) {
+            const float *k = p.keys + (long long)t * kvw + kvh * hd;
+            double dot = 0;
+            for (int j = 0; j < hd; ++j) dot = __dadd_rn(dot, __dmul_rn((double)q[j], (double)k[j]));
+            sbuf[threadIdx.x] = exp(__dsub_rn(__dmul_rn(dot, scale), mx));
+        }
+        __syncthreads();
+        const int n = min((int)blockDim.x, T - tc);
+        for (int r = 0; r < 2; ++r) {
+            const int d = threadIdx.x + r * blockDim.x;
+            if (d < hd)
+                for (int j = 0; j < n; ++j)
+                    sum[r] = __dadd_rn(sum[r], __dmul_rn(__ddiv_rn(sbuf[j], tot),
+                                                         (double)p.values[(long long)(tc + j) * kvw + kvh * hd + d]));
+        }
+        __syncthreads();
+    }
+    for (int r = 0; r < 2; ++r) {
+        const int d = threadIdx.x + r * blockDim.x;
+        if (d < hd) out[d] = (float)sum[r];
+    }
+}
+
+__global__ void __launch_bounds__(128) attn_merge_kernel(AttnParams p)
+{
+    extern __shared__ float wts[];  // [nsplit]
+    __shared__ int bad;
+    __shared__ double sbuf[128];
+    const int head = blockIdx.x;
+    const int hd = p.head_dim, rs = hd + 2;
+    if (p.use_pdl) pdl_wait();
+    if (threadIdx.x == 0) bad = 0;
+    __syncthreads();
+    const float *rec = p.scratch + (long long)head * rs;
+    const long long split_stride = (long long)p.q_heads * rs;
+    float m = -INFINITY;
+    for (int s = 0; s < p.nsplit; ++s) {
+        const float ms = rec[s * split_stride];
+        if (isnan(ms) || ms == INFINITY) bad = 1;
+        m = fmaxf(m, ms);
+    }
+    for (int s = threadIdx.x; s < p.nsplit; s += blockDim.x) {
+        const float ms = rec[s * split_stride];
+        wts[s] = ms == -INFINITY ? 0.0f : expf(ms - m);
+        if (!isfinite(rec[s * split_stride + 1])) bad = 1;
+    }
+    __syncthreads();
+    float l = 0.0f;
+    for (int s = 0; s < p.nsplit; ++s) l = fmaf(rec[s * split_stride + 1], wts[s], l);
+    float o[2] = {0.0f, 0.0f};
+    for (int r = 0; r < 2; ++r) {
+        const int d = threadIdx.x + r * blockDim.x;
+        if (d < hd) {
+            float a = 0.0f;
+            for (int s = 0; s < p.nsplit; ++s) a = fmaf(rec[s * split_stride + 2 + d], wts[s], a);
+            if (!isfinite(a)) bad = 1;
+            o[r] = a / l;
+        }
+    }
+    __syncthreads();
+    if (bad || !isfinite(l) || l <= 0.0f) {
+        const int T = p.tokens_dev ? *p.tokens_dev : p.tokens;
+        head_fp64(p, head, T, sbuf, p.out + (long long)head * hd);
+    } else {
+        for (int r = 0; r < 2; ++r) {
+            const int d = threadIdx.x + r * blockDim.x;
+            if (d < hd) p.out[(long long)head * hd + d] = o[r];
+        }
+    }
+    if (p.use_pdl) pdl_launch_dependents();
+}
+
+template <int DPL, bool VEC4, int GMAX>
+cudaError_t launch_partial(const AttnParams &p, dim3 grid, cudaStream_t stream)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kWarps * 32);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = p.use_pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, attn_partial_kernel<DPL, VEC4, GMAX>, p);
+}
+
+template <int DPL, bool VEC4>
+cudaError_t launch_partial_g(const AttnParams &p, int gmax, dim3 grid, cudaStream_t stream)
+{
+    switch (gmax) {
+    case 1: return launch_partial<DPL, VEC4, 1>(p, grid, stream);
+    case 2: return launch_partial<DPL, VEC4, 2>(p, grid, stream);
+    case 4: return launch_partial<DPL, VEC4, 4>(p, grid, stream);
+    default: return launch_partial<DPL, VEC4, 8>(p, grid, stream);
+    }
+}
+
+int gmax_for(int group) { return group >= 8 ? 8 : group > 2 ? (group > 4 ? 8 : 4) : group; }
+
+// ---------------------------------------------------------------- RoPE + append
+__global__ void rope_append_kernel(RopeAppendArgs a)
+{
+    if (a.use_pdl) pdl_wait();
+    const int pos = a.position_dev ? *a.position_dev : a.position;
+    const int hd = a.head_dim, half = a.rotary / 2;
+    const int qw = a.q_heads * hd, kvw = a.kv_heads * hd;
+    float *kslot = a.k_cache + (long long)pos * kvw;
+    float *vslot = a.v_cache + (long long)pos * kvw;
+    // TransformerOps.RopeHalf (TransformerOps.cs:99-118): FP64 angle and rotation, FP32 result.
+    for (int i = threadIdx.x; i < qw + 2 * kvw; i += blockDim.x) {
+        if (i < qw + kvw) {
+            const bool isq = i < qw;
+            const int e = isq ? i : i - qw;
+            const float *src = isq ? a.q : a.k;
+            float *dst = isq ? a.q_out : kslot;
+            const int d = e % hd, base_i = e - d;
+            float r;
+            if (d < a.rotary) {
+                const int k = d < half ? d : d - half;
+                const double angle = __ddiv_rn((double)pos, pow(a.base, __ddiv_rn(2.0 * k, (double)a.rotary)));
+                double sn, cs;
+                sincos(angle, &sn, &cs);
+                const double x = src[base_i + k], y = src[base_i + k + half];
+                r = d < half ? (float)__dsub_rn(__dmul_rn(x, cs), __dmul_rn(y, sn))
+                             : (float)__dadd_rn(__dmul_rn(x, sn), __dmul_rn(y, cs));
+            } else {
+                r = src[e];
+            }
+            dst[e] = r;
+        } else {
+            const int e = i - qw - kvw;
+            vslot[e] = a.v[e];
+        }
+    }
+    if (a.use_pdl) pdl_launch_dependents();
+}
+
+__global__ void rope_half_kernel(float *v, int n, int hd, int pos, double base, int rotary)
+{
+    const int half = rotary / 2;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n / hd * half; i += gridDim.x * blockDim.x) {
+        const int head = i / half, k = i - head * half;
+        const double angle = __ddiv_rn((double)pos, pow(base, __ddiv_rn(2.0 * k, (double)rotary)));
+        double sn, cs;
+        sincos(angle, &sn, &cs);
+        float *h = v + (long long)head * hd;
+        const double x = h[k], y = h[k + half];
+        h[k] = (float)__dsub_rn(__dmul_rn(x, cs), __dmul_rn(y, sn));
+        h[k + half] = (float)__dadd_rn(__dmul_rn(x, sn), __dmul_rn(y, cs));
+    }
+}
+
+}  // namespace
+
+int attn_splits(int q_heads, int kv_heads, int head_dim, int max_tokens, int sm_count)
+{
+    const int group = q_heads / kv_heads;
+    const int gmax = gmax_for(group);
+    const int ngroups = (group + gmax - 1) / gmax;
+    const int units = kv_heads * ngroups;
+    int nsplit = std::max(1, (3 * sm_count + units - 1) / units);
+    nsplit = std::min(nsplit, std::max(1, max_tokens / (2 * kTokBlock)));
+    (void)head_dim;
+    return nsplit;
+}
+
+size_t attn_scratch_floats(int q_heads, int kv_heads, int head_dim, int max_tokens, int sm_count)
+{
+    return (size_t)attn_splits(q_heads, kv_heads, head_dim, max_tokens, sm_count) * q_heads * (head_dim + 2);
+}
+
+cudaError_t launch_attention(const AttnArgs &a, int sm_count, cudaStream_t stream)
+{
+    if (a.head_dim <= 0 || a.head_dim > 256 || a.q_heads % a.kv_heads != 0) return cudaErrorInvalidValue;
+    AttnParams p;
+    p.q = a.q;
+    p.keys = a.keys;
+    p.values = a.values;
+    p.q_heads = a.q_heads;
+    p.kv_heads = a.kv_heads;
+    p.head_dim = a.head_dim;
+    p.group = a.q_heads / a.kv_heads;
+    const int gmax = gmax_for(p.group);
+    p.ngroups = (p.group + gmax - 1) / gmax;
+    p.tokens = a.tokens;
+    p.tokens_dev = a.tokens_dev;
+    p.nsplit = attn_splits(a.q_heads, a.kv_heads, a.head_dim, a.max_tokens, sm_count);
+    p.scale = (float)(1.0 / std::sqrt((double)a.head_dim));
+    p.scratch = a.scratch;
+    p.out = a.out;
+    p.use_pdl = a.use_pdl;
+    const dim3 grid(p.nsplit, a.kv_heads * p.ngroups);
+    cudaError_t e;
+    if (a.head_dim == 128) e = launch_partial_g<4, true>(p, gmax, grid, stream);
+    else e = launch_partial_g<8, false>(p, gmax, grid, stream);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.q_heads);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = sizeof(float) * (size_t)p.nsplit;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = a.use_pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, attn_merge_kernel, p);
+}
+
+cudaError_t launch_rope_append(const RopeAppendArgs &a, cudaStream_t stream)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(512);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = a.use_pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, rope_append_kernel, a);
+}
+
+cudaError_t launch_rope_half(float *v, int n, int head_dim, int position, double base, int rotary,
+                             cudaStream_t stream)
+{
+    rope_half_kernel<<<4, 256, 0, stream>>>(v, n, head_dim, position, base, rotary);
+    return cudaGetLastError();
+}
+
+}  // namespace satori

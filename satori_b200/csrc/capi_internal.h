@@ -1,0 +1,53 @@
+// capi_internal.h -- shared host-side state of the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/satori_cuda.h"
+
+struct satori_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;     // current stream (own or caller's)
+    cudaStream_t own_stream = nullptr;
+    int sm_count = 0;
+    size_t smem_optin = 0;
+    unsigned *d_err = nullptr;         // device error word (bounded waits)
+    int *d_status = nullptr;           // validation status scratch
+    float *attn_scratch = nullptr;     // grow-only partial records for one-shot attention calls
+    size_t attn_scratch_floats = 0;
+};
+
+struct satori_matrix {
+    satori_ctx *ctx = nullptr;
+    uint8_t *d_payload = nullptr;
+    size_t bytes = 0;
+    int rows = 0, cols = 0, format = 0;
+    float *d_x = nullptr, *d_y = nullptr;     // device work vectors for host-pointer calls
+    float *h_x = nullptr, *h_y = nullptr;     // pinned staging
+    size_t cap_positions = 0;
+};
+
+namespace satori {
+
+int set_error(int status, const char *fmt, ...);
+int cuda_fail(cudaError_t e, const char *what);
+// Clears the context's device error word on its stream.
+cudaError_t clear_dev_error(satori_ctx *ctx);
+// Reads the device error word (synchronises the stream) and maps it to a status.
+int check_dev_error(satori_ctx *ctx);
+bool is_valid_format(int format);
+size_t payload_bytes(int rows, int cols, int format);
+int validate_shape(int rows, int cols, int format);
+// Uploads and validates a payload; on success *out owns a device copy padded for bulk copies.
+int upload_payload(satori_ctx *ctx, const uint8_t *src, bool src_is_device, size_t bytes, int rows, int cols,
+                   int format, uint8_t **out);
+// Runs the MatVec on device pointers with the library's plan for this shape.
+int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int format, int order,
+             const float *dx, float *dy, int positions, int epilogue, const float *bias, float *residual,
+             cudaStream_t stream, int use_pdl);
+
+}  // namespace satori

@@ -1,0 +1,118 @@
+// common.cuh -- shared device helpers for the sm_100a decode kernels.
+//
+// Arithmetic helpers use the _rn intrinsics so nvcc never contracts or reorders them: the
+// kernels reproduce the reference's FP32 operation order bit for bit.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/satori_cuda.h"
+
+namespace satori {
+
+// --------------------------------------------------------------------------- error flags
+// Device-side error word of a context: bit 0 = a bounded wait expired.
+enum : unsigned { kDevErrTimeout = 1u };
+
+// Spin budget for mbarrier waits: ~4e9 cycles of polling is seconds, far beyond any copy.
+constexpr long long kWaitBudgetCycles = 4000000000LL;
+
+// --------------------------------------------------------------------------- exact FP32 ops
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float ffma(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+
+// The SSE horizontal sum every reference AVX2 kernel ends a block with
+// (QuantizedKAvx2Kernel.cs:341-347): ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)).
+__device__ __forceinline__ float hsum8(const float a[8])
+{
+    float h0 = fadd(a[0], a[4]), h1 = fadd(a[1], a[5]), h2 = fadd(a[2], a[6]), h3 = fadd(a[3], a[7]);
+    return fadd(fadd(h0, h2), fadd(h1, h3));
+}
+
+// Exact small-integer -> float conversion through the 2^23 exponent trick: (float)v - bias, v < 2^23.
+__device__ __forceinline__ float u8_to_f_minus(uint32_t v, float bias)
+{
+    return __fsub_rn(__uint_as_float(0x4B000000u | v), 8388608.0f + bias);
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t bits16)
+{
+    return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFFu)));
+}
+
+// --------------------------------------------------------------------------- shared memory
+__device__ __forceinline__ uint32_t smem_u32(const void *p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr)
+{
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ float4 lds128f(uint32_t addr)
+{
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+
+// --------------------------------------------------------------------------- mbarrier + bulk copy
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: returns false (and the caller records a timeout) if the phase never flips.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    long long start = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - start > kWaitBudgetCycles) return false;
+    }
+    return true;
+}
+
+// 1-D bulk copy global -> shared (TMA unicast, no multicast), completing on `bar`.
+// dst, src and bytes must all be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+// --------------------------------------------------------------------------- PDL
+// Programmatic dependent launch: wait for the producer grid's memory to be visible / let the
+// next grid start its prologue.  Both are no-ops when the launch did not use PDL.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+}  // namespace satori

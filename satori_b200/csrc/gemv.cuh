@@ -1,0 +1,55 @@
+// gemv.cuh -- quantized MatVec (Q8_0, Q4_0, Ternary2) launch interface.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace satori {
+
+// Optional fused epilogue of the MatVec (decode-step glue; each reproduces the reference op):
+//   y = acc                       (kEpiNone)
+//   y = acc + bias                (kEpiBias: TransformerOps.Add(query, bias, query), DenseForward.cs:124-129)
+//   y = residual + acc, residual := y  (kEpiResidual: TransformerOps.Add(residual, projected, residual),
+//                                      DenseForward.cs:148,160)
+enum Epilogue : int { kEpiNone = 0, kEpiBias = 1, kEpiResidual = 2 };
+
+struct GemvArgs {
+    const uint8_t *payload;  // device, 256-byte aligned, readable 16 bytes past the end
+    int rows, cols, format;  // format: 0 Q8_0, 1 Q4_0, 64/128/256 Ternary2
+    int order;               // satori_order
+    const float *x;          // device [positions][cols]
+    float *y;                // device [positions][rows]
+    int positions;
+    int epilogue;
+    const float *bias;       // [rows] for kEpiBias
+    float *residual;         // [rows] for kEpiResidual (positions == 1)
+    unsigned *err;           // device error word
+    int use_pdl;             // launched with programmatic stream serialization
+};
+
+// Geometry the host chooses for one launch.
+struct GemvPlan {
+    int grid, threads, rows_per_cta, chunk_blocks, nchunks, stages, seg_stride, dstride;
+    size_t smem;
+    int ok;
+};
+
+GemvPlan plan_gemv(int rows, int cols, int format, int positions, int sm_count, size_t smem_limit);
+cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &plan, cudaStream_t stream);
+int gemv_block_bytes(int format);
+int gemv_block_elems(int format);
+
+// Row decode (GgufQuantizedMatrix.ReadRow / Ternary2Matrix.Dequantize), device pointers.
+cudaError_t launch_decode_row(const uint8_t *payload, int rows, int cols, int format, const int *row_dev,
+                              int row_host, float *out, cudaStream_t stream);
+
+// Payload validation on the device: writes 0 or a satori_status into *status_dev.
+cudaError_t launch_validate(const uint8_t *payload, int rows, int cols, int format, int *status_dev,
+                            cudaStream_t stream);
+
+// Ternary2Matrix.Quantize on the device (bit-exact), and this library's own Q8_0/Q4_0 quantizer.
+cudaError_t launch_t2_quantize(const float *w, int rows, int cols, int bs, uint8_t *out, int *status_dev,
+                               cudaStream_t stream);
+cudaError_t launch_q_quantize(const float *w, int rows, int cols, int format, uint8_t *out, cudaStream_t stream);
+
+}  // namespace satori

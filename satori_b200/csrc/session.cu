@@ -1,0 +1,420 @@
+// session.cu -- the dense decode session: DenseSession.Append (src/Satori.Core/Model/DenseSession.cs:111-131)
+// with DenseForward.Embed/Step/Final (src/Satori.Core/Model/DenseForward.cs:87-162, 298-306) and greedy
+// selection, entirely on the device.
+//
+// All weights are uploaded once at creation (unchanged GGUF layout) and the KV cache lives in HBM
+// ([layer][context][kv_heads*head_dim], DenseSession.cs:80-84).  One decode step is a fixed
+// sequence of kernels whose only varying inputs -- the token and the position -- live in device
+// memory, so the step is captured once into a CUDA graph and replayed for every token; the greedy
+// argmax kernel writes the next token and advances the position on the device, so a generation
+// loop needs no host round trip between tokens.
+#include "attention.cuh"
+#include "capi_internal.h"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "ops.cuh"
+#include "session_internal.h"
+
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+using namespace satori;
+
+#define TRY(x)               \
+    do {                     \
+        int rc_ = (x);       \
+        if (rc_) return rc_; \
+    } while (0)
+#define TRYCUDA(x, what)                                   \
+    do {                                                   \
+        cudaError_t e_ = (x);                              \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+namespace {
+
+const satori_tensor *find_tensor(const satori_model_desc *d, const std::string &name)
+{
+    for (int i = 0; i < d->n_tensors; ++i)
+        if (d->tensors[i].name && name == d->tensors[i].name) return &d->tensors[i];
+    return nullptr;
+}
+
+int fetch_matrix(satori_session *s, const satori_model_desc *d, const std::string &name, int rows, int cols,
+                 DevMatrix *out)
+{
+    const satori_tensor *t = find_tensor(d, name);
+    if (!t) return set_error(SATORI_ERR_ARGUMENT, "missing tensor %s", name.c_str());
+    if (t->format < 0 || t->rows != rows || t->cols != cols)
+        return set_error(SATORI_ERR_ARGUMENT, "tensor %s has shape %dx%d (format %d), expected %dx%d matrix",
+                         name.c_str(), t->rows, t->cols, t->format, rows, cols);
+    if (t->bytes != payload_bytes(rows, cols, t->format))
+        return set_error(SATORI_ERR_ARGUMENT, "tensor %s has %zu bytes, expected %zu", name.c_str(), t->bytes,
+                         payload_bytes(rows, cols, t->format));
+    uint8_t *dp = nullptr;
+    TRY(upload_payload(s->ctx, (const uint8_t *)t->data, false, t->bytes, rows, cols, t->format, &dp));
+    s->allocations.push_back(dp);
+    out->payload = dp;
+    out->rows = rows;
+    out->cols = cols;
+    out->format = t->format;
+    s->weight_bytes += t->bytes;
+    return SATORI_OK;
+}
+
+int fetch_vector(satori_session *s, const satori_model_desc *d, const std::string &name, int n, float **out,
+                 bool optional = false)
+{
+    const satori_tensor *t = find_tensor(d, name);
+    if (!t) {
+        if (optional) {
+            *out = nullptr;
+            return SATORI_OK;
+        }
+        return set_error(SATORI_ERR_ARGUMENT, "missing tensor %s", name.c_str());
+    }
+    if (t->format != -1 || t->rows != n || t->bytes != (size_t)n * 4)
+        return set_error(SATORI_ERR_ARGUMENT, "tensor %s must be %d float32 values", name.c_str(), n);
+    float *dv = nullptr;
+    TRYCUDA(cudaMalloc(&dv, (size_t)n * 4), "upload vector");
+    s->allocations.push_back(dv);
+    TRYCUDA(cudaMemcpy(dv, t->data, (size_t)n * 4, cudaMemcpyDefault), "upload vector");
+    *out = dv;
+    return SATORI_OK;
+}
+
+template <typename T>
+int dalloc(satori_session *s, T **p, size_t n)
+{
+    TRYCUDA(cudaMalloc(p, n * sizeof(T) + 16), "allocate session buffer");
+    s->allocations.push_back(*p);
+    TRYCUDA(cudaMemset(*p, 0, n * sizeof(T) + 16), "clear session buffer");
+    return SATORI_OK;
+}
+
+}  // namespace
+
+// Enqueues one decode step on `st` (captured into the graph).
+static int enqueue_step(satori_session *s, cudaStream_t st)
+{
+    const int pdl = s->use_pdl;
+    const int H = s->hidden, F = s->ffn, qw = s->q_width, kvw = s->kv_width;
+    TRYCUDA(launch_embed(s->embd.payload, H, s->d_token, s->d_pos, s->d_tokens, s->d_hidden, st, pdl), "embed");
+    for (int l = 0; l < s->layers; ++l) {
+        const Layer &L = s->layer[l];
+        TRYCUDA(launch_rmsnorm(s->d_hidden, L.attn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
+        TRY(run_gemv(s->ctx, L.q.payload, L.q.rows, H, L.q.format, SATORI_ORDER_BATCH, s->d_normed, s->d_q, 1,
+                     L.q_bias ? kEpiBias : kEpiNone, L.q_bias, nullptr, st, pdl));
+        TRY(run_gemv(s->ctx, L.k.payload, L.k.rows, H, L.k.format, SATORI_ORDER_BATCH, s->d_normed, s->d_k, 1,
+                     L.k_bias ? kEpiBias : kEpiNone, L.k_bias, nullptr, st, pdl));
+        TRY(run_gemv(s->ctx, L.v.payload, L.v.rows, H, L.v.format, SATORI_ORDER_BATCH, s->d_normed, s->d_v, 1,
+                     L.v_bias ? kEpiBias : kEpiNone, L.v_bias, nullptr, st, pdl));
+        if (L.q_norm) {
+            TRYCUDA(launch_rmsnorm_heads(s->d_q, qw, L.q_norm, s->eps, s->head_dim, st, pdl), "q norm");
+            TRYCUDA(launch_rmsnorm_heads(s->d_k, kvw, L.k_norm, s->eps, s->head_dim, st, pdl), "k norm");
+        }
+        RopeAppendArgs r = {};
+        r.q = s->d_q;
+        r.k = s->d_k;
+        r.v = s->d_v;
+        r.q_out = s->d_qrot;
+        r.k_cache = s->d_kcache + (size_t)l * s->context * kvw;
+        r.v_cache = s->d_vcache + (size_t)l * s->context * kvw;
+        r.q_heads = s->q_heads;
+        r.kv_heads = s->kv_heads;
+        r.head_dim = s->head_dim;
+        r.rotary = s->head_dim;
+        r.base = s->rope_base;
+        r.position_dev = s->d_pos;
+        r.use_pdl = pdl;
+        TRYCUDA(launch_rope_append(r, st), "rope/append");
+        AttnArgs a = {};
+        a.q = s->d_qrot;
+        a.keys = r.k_cache;
+        a.values = r.v_cache;
+        a.q_heads = s->q_heads;
+        a.kv_heads = s->kv_heads;
+        a.head_dim = s->head_dim;
+        a.tokens_dev = s->d_tokens;
+        a.max_tokens = s->context;
+        a.out = s->d_ctx;
+        a.scratch = s->d_attn_scratch;
+        a.err = s->ctx->d_err;
+        a.use_pdl = pdl;
+        TRYCUDA(launch_attention(a, s->ctx->sm_count, st), "attention");
+        TRY(run_gemv(s->ctx, L.o.payload, H, qw, L.o.format, SATORI_ORDER_BATCH, s->d_ctx, s->d_proj, 1, kEpiResidual,
+                     nullptr, s->d_hidden, st, pdl));
+        TRYCUDA(launch_rmsnorm(s->d_hidden, L.ffn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
+        TRY(run_gemv(s->ctx, L.gate.payload, F, H, L.gate.format, SATORI_ORDER_BATCH, s->d_normed, s->d_gate, 1,
+                     kEpiNone, nullptr, nullptr, st, pdl));
+        TRY(run_gemv(s->ctx, L.up.payload, F, H, L.up.format, SATORI_ORDER_BATCH, s->d_normed, s->d_up, 1, kEpiNone,
+                     nullptr, nullptr, st, pdl));
+        TRYCUDA(launch_swiglu(s->d_gate, s->d_up, F, s->d_act, st, pdl), "swiglu");
+        TRY(run_gemv(s->ctx, L.down.payload, H, F, L.down.format, SATORI_ORDER_BATCH, s->d_act, s->d_proj, 1,
+                     kEpiResidual, nullptr, s->d_hidden, st, pdl));
+    }
+    TRYCUDA(launch_rmsnorm(s->d_hidden, s->output_norm, H, s->eps, s->d_final, st, pdl), "final norm");
+    TRY(run_gemv(s->ctx, s->output.payload, s->vocab, H, s->output.format, SATORI_ORDER_BATCH, s->d_final, s->d_logits,
+                 1, kEpiNone, nullptr, nullptr, st, pdl));
+    TRYCUDA(launch_argmax_advance(s->d_logits, s->vocab, s->d_argmax, s->d_nonfinite, s->d_pos, s->d_token, st, pdl),
+            "argmax");
+    return SATORI_OK;
+}
+
+static int build_graph(satori_session *s)
+{
+    cudaStream_t st = s->ctx->stream;
+    TRYCUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture");
+    int rc = enqueue_step(s, st);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "end capture");
+    e = cudaGraphInstantiate(&s->graph_exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(e, "instantiate graph");
+    return SATORI_OK;
+}
+
+static int session_upload(satori_session *s, const satori_model_desc *d)
+{
+    const int H = d->hidden, F = d->ffn;
+    s->layer.resize(d->layers);
+    for (int l = 0; l < d->layers; ++l) {
+        Layer &L = s->layer[l];
+        const std::string p = "blk." + std::to_string(l) + ".";
+        TRY(fetch_vector(s, d, p + "attn_norm.weight", H, &L.attn_norm));
+        TRY(fetch_vector(s, d, p + "ffn_norm.weight", H, &L.ffn_norm));
+        TRY(fetch_matrix(s, d, p + "attn_q.weight", s->q_width, H, &L.q));
+        TRY(fetch_matrix(s, d, p + "attn_k.weight", s->kv_width, H, &L.k));
+        TRY(fetch_matrix(s, d, p + "attn_v.weight", s->kv_width, H, &L.v));
+        TRY(fetch_matrix(s, d, p + "attn_output.weight", H, s->q_width, &L.o));
+        TRY(fetch_matrix(s, d, p + "ffn_gate.weight", F, H, &L.gate));
+        TRY(fetch_matrix(s, d, p + "ffn_up.weight", F, H, &L.up));
+        TRY(fetch_matrix(s, d, p + "ffn_down.weight", H, F, &L.down));
+        TRY(fetch_vector(s, d, p + "attn_q.bias", s->q_width, &L.q_bias, true));
+        TRY(fetch_vector(s, d, p + "attn_k.bias", s->kv_width, &L.k_bias, true));
+        TRY(fetch_vector(s, d, p + "attn_v.bias", s->kv_width, &L.v_bias, true));
+        // Qwen2 carries all three biases or none; a partial set is rejected.
+        if (!!L.q_bias != !!L.k_bias || !!L.q_bias != !!L.v_bias)
+            return set_error(SATORI_ERR_ARGUMENT, "layer %d has a partial q/k/v bias set", l);
+        TRY(fetch_vector(s, d, p + "attn_q_norm.weight", s->head_dim, &L.q_norm, true));
+        TRY(fetch_vector(s, d, p + "attn_k_norm.weight", s->head_dim, &L.k_norm, true));
+        if (!!L.q_norm != !!L.k_norm) return set_error(SATORI_ERR_ARGUMENT, "layer %d has a partial q/k norm set", l);
+    }
+    const satori_tensor *e = find_tensor(d, "token_embd.weight");
+    // GgufQuantizedMatrix.ReadRow rejects Q4_0 embedding rows (GgufQuantizedMatrix.cs:56).
+    if (e && e->format == SATORI_Q4_0)
+        return set_error(SATORI_ERR_NOT_SUPPORTED, "Q4_0 embedding rows are not supported");
+    TRY(fetch_matrix(s, d, "token_embd.weight", d->vocab, H, &s->embd));
+    if (s->embd.format != SATORI_Q8_0)
+        return set_error(SATORI_ERR_NOT_SUPPORTED, "embedding rows must be Q8_0");
+    TRY(fetch_vector(s, d, "output_norm.weight", H, &s->output_norm));
+    if (d->tied_embeddings) s->output = s->embd;
+    else TRY(fetch_matrix(s, d, "output.weight", d->vocab, H, &s->output));
+    return SATORI_OK;
+}
+
+int session_alloc_state(satori_session *s)
+{
+    const size_t kv = (size_t)s->layers * s->context * s->kv_width;
+    TRY(dalloc(s, &s->d_kcache, kv));
+    TRY(dalloc(s, &s->d_vcache, kv));
+    TRY(dalloc(s, &s->d_hidden, s->hidden));
+    TRY(dalloc(s, &s->d_normed, s->hidden));
+    TRY(dalloc(s, &s->d_final, s->hidden));
+    TRY(dalloc(s, &s->d_proj, s->hidden));
+    TRY(dalloc(s, &s->d_q, s->q_width));
+    TRY(dalloc(s, &s->d_qrot, s->q_width));
+    TRY(dalloc(s, &s->d_ctx, s->q_width));
+    TRY(dalloc(s, &s->d_k, s->kv_width));
+    TRY(dalloc(s, &s->d_v, s->kv_width));
+    TRY(dalloc(s, &s->d_gate, s->ffn));
+    TRY(dalloc(s, &s->d_up, s->ffn));
+    TRY(dalloc(s, &s->d_act, s->ffn));
+    TRY(dalloc(s, &s->d_logits, s->vocab));
+    TRY(dalloc(s, &s->d_ints, 8));
+    s->d_token = s->d_ints + 0;
+    s->d_pos = s->d_ints + 1;
+    s->d_tokens = s->d_ints + 2;
+    s->d_argmax = s->d_ints + 3;
+    s->d_nonfinite = s->d_ints + 4;
+    TRY(dalloc(s, &s->d_attn_scratch,
+               attn_scratch_floats(s->q_heads, s->kv_heads, s->head_dim, s->context, s->ctx->sm_count)));
+    TRYCUDA(cudaHostAlloc(&s->h_ints, 8 * sizeof(int), cudaHostAllocDefault), "pinned ints");
+    TRYCUDA(cudaHostAlloc(&s->h_logits, (size_t)s->vocab * 4, cudaHostAllocDefault), "pinned logits");
+    return SATORI_OK;
+}
+
+static int check_desc(const satori_model_desc *d, int context)
+{
+    if (!d) return set_error(SATORI_ERR_ARGUMENT, "desc is null");
+    if (d->layers <= 0 || d->hidden <= 0 || d->ffn <= 0 || d->q_heads <= 0 || d->kv_heads <= 0 || d->head_dim <= 0 ||
+        d->vocab <= 0 || context <= 0)
+        return set_error(SATORI_ERR_ARGUMENT, "model dimensions and context must be positive");
+    if (d->q_heads % d->kv_heads != 0) return set_error(SATORI_ERR_ARGUMENT, "q_heads must be a multiple of kv_heads");
+    if (d->head_dim % 2 != 0 || d->head_dim > 256) return set_error(SATORI_ERR_ARGUMENT, "unsupported head_dim");
+    if (!(d->rms_epsilon > 0) || !(d->rope_base > 0)) return set_error(SATORI_ERR_ARGUMENT, "bad epsilon/rope base");
+    return SATORI_OK;
+}
+
+extern "C" int satori_session_create(satori_ctx *ctx, const satori_model_desc *d, int context, satori_session **out)
+{
+    if (!ctx || !out) return set_error(SATORI_ERR_ARGUMENT, "null argument");
+    TRY(check_desc(d, context));
+    satori_session *s = new satori_session();
+    s->ctx = ctx;
+    s->layers = d->layers;
+    s->hidden = d->hidden;
+    s->ffn = d->ffn;
+    s->q_heads = d->q_heads;
+    s->kv_heads = d->kv_heads;
+    s->head_dim = d->head_dim;
+    s->vocab = d->vocab;
+    s->eps = d->rms_epsilon;
+    s->rope_base = d->rope_base;
+    s->context = context;
+    s->q_width = d->q_heads * d->head_dim;
+    s->kv_width = d->kv_heads * d->head_dim;
+    s->use_pdl = 1;
+    int rc = session_upload(s, d);
+    if (!rc) rc = session_alloc_state(s);
+    if (!rc) rc = build_graph(s);
+    if (rc) {
+        char buf[512];
+        satori_last_error(buf, sizeof buf);
+        std::string msg = buf;
+        satori_session_destroy(s);
+        return set_error(rc, "%s", msg.c_str());
+    }
+    *out = s;
+    return SATORI_OK;
+}
+
+// Runs `count` steps fed from host tokens `feed` (one step per token).
+static int run_steps(satori_session *s, const int *feed, int count, float *logits, int *argmax)
+{
+    if (!s) return set_error(SATORI_ERR_DISPOSED, "session is disposed");
+    if (count <= 0) return set_error(SATORI_ERR_ARGUMENT, "count must be positive");
+    for (int i = 0; i < count; ++i)
+        if (feed[i] < 0 || feed[i] >= s->vocab)
+            return set_error(SATORI_ERR_ARGUMENT, "Token %d is outside the vocabulary.", feed[i]);
+    if (s->position + count > s->context)
+        return set_error(SATORI_ERR_CONTEXT_FULL, "Context limit %d reached; reset or enlarge the session.", s->context);
+    satori_ctx *ctx = s->ctx;
+    cudaStream_t st = ctx->stream;
+    TRYCUDA(clear_dev_error(ctx), "clear error");
+    for (int i = 0; i < count; ++i) {
+        s->h_ints[7] = feed[i];
+        TRYCUDA(cudaMemcpyAsync(s->d_token, &s->h_ints[7], sizeof(int), cudaMemcpyHostToDevice, st), "token");
+        TRYCUDA(cudaGraphLaunch(s->graph_exec, st), "graph launch");
+        // The pinned token slot is reused by the next step: wait until this one has been read.
+        if (i + 1 < count) TRYCUDA(cudaStreamSynchronize(st), "sync");
+    }
+    TRYCUDA(cudaMemcpyAsync(s->h_ints, s->d_ints, 7 * sizeof(int), cudaMemcpyDeviceToHost, st), "state");
+    if (logits)
+        TRYCUDA(cudaMemcpyAsync(s->h_logits, s->d_logits, (size_t)s->vocab * 4, cudaMemcpyDeviceToHost, st), "logits");
+    int rc = check_dev_error(ctx);
+    s->position += count;
+    if (rc) return rc;
+    if (s->h_ints[4]) {
+        cudaMemsetAsync(s->d_nonfinite, 0, sizeof(int), st);
+        return set_error(SATORI_ERR_INVALID_DATA, "Non-finite logit.");
+    }
+    if (logits) memcpy(logits, s->h_logits, (size_t)s->vocab * 4);
+    if (argmax) *argmax = s->h_ints[3];
+    return SATORI_OK;
+}
+
+extern "C" int satori_session_append(satori_session *s, int token, float *logits, int *argmax)
+{
+    return run_steps(s, &token, 1, logits, argmax);
+}
+
+extern "C" int satori_session_append_tokens(satori_session *s, const int *tokens, int count, float *logits, int *argmax)
+{
+    if (!tokens) return set_error(SATORI_ERR_ARGUMENT, "tokens is null");
+    return run_steps(s, tokens, count, logits, argmax);
+}
+
+extern "C" int satori_session_generate(satori_session *s, int first, int count, int *tokens_out)
+{
+    if (!s) return set_error(SATORI_ERR_DISPOSED, "session is disposed");
+    if (!tokens_out) return set_error(SATORI_ERR_ARGUMENT, "tokens_out is null");
+    if (first < 0 || first >= s->vocab) return set_error(SATORI_ERR_ARGUMENT, "Token %d is outside the vocabulary.", first);
+    if (count <= 0) return set_error(SATORI_ERR_ARGUMENT, "count must be positive");
+    if (s->position + count > s->context)
+        return set_error(SATORI_ERR_CONTEXT_FULL, "Context limit %d reached; reset or enlarge the session.", s->context);
+    cudaStream_t st = s->ctx->stream;
+    std::vector<int> out(count);
+    int *d_out = nullptr;
+    TRYCUDA(cudaMalloc(&d_out, sizeof(int) * count), "alloc tokens");
+    s->h_ints[7] = first;
+    cudaError_t e = cudaMemcpyAsync(s->d_token, &s->h_ints[7], sizeof(int), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = clear_dev_error(s->ctx);
+    // First step consumes `first`; later steps consume the device-side argmax of the step before.
+    for (int i = 0; i < count && e == cudaSuccess; ++i) {
+        e = cudaGraphLaunch(s->graph_exec, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(d_out + i, s->d_argmax, sizeof(int), cudaMemcpyDeviceToDevice, st);
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out.data(), d_out, sizeof(int) * count, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->h_ints, s->d_ints, 7 * sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaFree(d_out);
+    if (e != cudaSuccess) return cuda_fail(e, "generate");
+    int rc = check_dev_error(s->ctx);
+    s->position += count;
+    if (rc) return rc;
+    if (s->h_ints[4]) {
+        cudaMemsetAsync(s->d_nonfinite, 0, sizeof(int), st);
+        return set_error(SATORI_ERR_INVALID_DATA, "Non-finite logit.");
+    }
+    memcpy(tokens_out, out.data(), sizeof(int) * count);
+    return SATORI_OK;
+}
+
+extern "C" int satori_session_position(const satori_session *s, int *position)
+{
+    if (!s) return set_error(SATORI_ERR_DISPOSED, "session is disposed");
+    if (position) *position = s->position;
+    return SATORI_OK;
+}
+
+extern "C" int satori_session_reset(satori_session *s)
+{
+    if (!s) return set_error(SATORI_ERR_DISPOSED, "session is disposed");
+    s->position = 0;
+    cudaError_t e = cudaMemsetAsync(s->d_pos, 0, sizeof(int), s->ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->ctx->stream);
+    return e == cudaSuccess ? SATORI_OK : cuda_fail(e, "reset");
+}
+
+extern "C" int satori_session_stage(const satori_session *s, int which, float *out, size_t n)
+{
+    if (!s) return set_error(SATORI_ERR_DISPOSED, "session is disposed");
+    const float *src = which == 0 ? s->d_hidden : which == 1 ? s->d_final : which == 2 ? s->d_logits : nullptr;
+    const size_t len = which == 2 ? (size_t)s->vocab : (size_t)s->hidden;
+    if (!src || !out || n != len) return set_error(SATORI_ERR_ARGUMENT, "bad stage %d / length %zu", which, n);
+    cudaError_t e = cudaMemcpyAsync(out, src, len * 4, cudaMemcpyDeviceToHost, s->ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->ctx->stream);
+    return e == cudaSuccess ? SATORI_OK : cuda_fail(e, "stage");
+}
+
+extern "C" int satori_session_destroy(satori_session *s)
+{
+    if (!s) return SATORI_OK;
+    cudaSetDevice(s->ctx->device);
+    cudaStreamSynchronize(s->ctx->stream);
+    if (s->graph_exec) cudaGraphExecDestroy(s->graph_exec);
+    session_destroy_sharding(s);
+    for (void *p : s->allocations) cudaFree(p);
+    if (s->h_ints) cudaFreeHost(s->h_ints);
+    if (s->h_logits) cudaFreeHost(s->h_logits);
+    delete s;
+    return SATORI_OK;
+}
