@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(Geo g)
         if (!is_chain && c < g.nchunks) {
             const int s = c % S;
             const int nb = min(g.cb, g.bpr - c * g.cb);
-            if (!mbar_wait_bounded(&full[s], (uint32_t)((c / S) & 1))) {
+            if (!abort_flag && !mbar_wait_bounded(&full[s], (uint32_t)((c / S) & 1))) {
                 atomicOr(g.err, kDevErrTimeout);
                 abort_flag = 1;
             }
