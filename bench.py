@@ -141,6 +141,7 @@ def device_quantized(ctx, rows, cols, fmt, seed, sigma=0.02):
     w = torch.randn(rows * cols, generator=g, device="cuda", dtype=torch.float32) * sigma
     bb = 34 if fmt == 0 else 18
     out = torch.empty(rows * (cols // 32) * bb, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()  # the quantizer runs on the library's stream, not torch's
     _lib.check(_lib.lib().satori_quantize_q_device(ctx.handle, w.data_ptr(), rows, cols, fmt, out.data_ptr()),
                "quantize")
     ctx.synchronize()
@@ -184,6 +185,7 @@ def bench_matvec(args, rank, world, local):
     gen = torch.Generator(device="cuda").manual_seed(77)
     x = torch.randn(4096, generator=gen, device="cuda", dtype=torch.float32)
     y = torch.empty(11008, device="cuda", dtype=torch.float32)
+    torch.cuda.synchronize()
     stream = torch.cuda.Stream()
     ctx.set_stream(stream.cuda_stream)
 
@@ -291,6 +293,7 @@ def bench_attention(args, rank, world, local):
     vc = torch.randn(layers, T * kvh * hd, generator=gen, device="cuda")
     q = torch.randn(qh * hd, generator=gen, device="cuda")
     out = torch.empty(qh * hd, device="cuda")
+    torch.cuda.synchronize()
     stream = torch.cuda.Stream()
     ctx.set_stream(stream.cuda_stream)
     L = _lib.lib()
@@ -354,6 +357,7 @@ def bench_ternary(args, rank, world, local):
         mats.append(sat.CudaQuantizedMatrix.from_device(ctx, src.device_payload, nbytes, n, n, bs))
     x = torch.randn(n, device="cuda")
     y = torch.empty(n, device="cuda")
+    torch.cuda.synchronize()
     stream = torch.cuda.Stream()
     ctx.set_stream(stream.cuda_stream)
     order = _lib.ORDER_EXECUTE if args.order == "execute" else _lib.ORDER_SCALAR
@@ -409,6 +413,7 @@ def bench_decode(args, rank, world, local, spec):
     ctx = sat.Context(local)
     context = args.prompt + args.decode + 8
     tensors = device_model(ctx, spec, seed=31)
+    torch.cuda.synchronize()
     sess = sat.CudaDenseSession(spec, tensors, context, ctx=ctx)
     del tensors
     torch.cuda.empty_cache()

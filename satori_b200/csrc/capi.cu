@@ -36,10 +36,9 @@ int set_error(int status, const char *fmt, ...)
 
 int cuda_fail(cudaError_t e, const char *what)
 {
-    if (e == cudaErrorMemoryAllocation) {
-        cudaGetLastError();
+    cudaGetLastError();  // clear a non-sticky error so it does not surface in a later, unrelated call
+    if (e == cudaErrorMemoryAllocation)
         return set_error(SATORI_ERR_OUT_OF_MEMORY, "%s: %s", what, cudaGetErrorString(e));
-    }
     return set_error(SATORI_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 

@@ -355,11 +355,12 @@ template <int FMT, int ORDER, int PMAX = 1>
 cudaError_t launch_one(const Geo &g, const GemvPlan &plan, cudaStream_t stream)
 {
     auto kern = gemv_kernel<FMT, ORDER, PMAX>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    // Opt in to exactly the dynamic shared memory this plan needs (the limit counts static smem too).
+    static size_t configured = 48 * 1024;
+    if (plan.smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
         if (e != cudaSuccess) return e;
-        configured = true;
+        configured = plan.smem;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(plan.grid);
