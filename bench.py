@@ -154,10 +154,11 @@ def events_time(fn, stream, steps: int) -> float:
     import torch
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
-    start.record(stream)
-    for _ in range(steps):
-        fn()
-    end.record(stream)
+    with torch.cuda.stream(stream):  # CUDAGraph.replay() launches on the current stream
+        start.record(stream)
+        for _ in range(steps):
+            fn()
+        end.record(stream)
     torch.cuda.synchronize()
     return start.elapsed_time(end)
 

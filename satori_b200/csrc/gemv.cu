@@ -138,6 +138,70 @@ __device__ __forceinline__ void q_terms(const uint32_t qw[8], float d, uint32_t 
     }
 }
 
+// ---------------------------------------------------------------- decode-order fast path
+// Dequantization in one FMA: PRMT places a code byte (biased int8, or a masked nibble) in bits 8..15
+// under the 2^23 exponent, giving f = 2^23 + 256*u.  Then fma(f, d/256, -d*(2^15 + bias)) equals
+// d*(u - bias) exactly: d has at most 11 significant bits, so d/256 and d*(2^15 + bias) are exact
+// FP32 values, and the exact result d*(u - bias) is representable, so the single rounding is a no-op.
+// This is the same value QuantizedRow.DecodeQ8Block/DecodeQ4Block computes as scale * code.
+__device__ __forceinline__ float2 f2pair(uint32_t word, uint32_t sel_lo, uint32_t sel_hi)
+{
+    return make_float2(__uint_as_float(__byte_perm(word, 0x4B000000u, sel_lo)),
+                       __uint_as_float(__byte_perm(word, 0x4B000000u, sel_hi)));
+}
+
+// Selector putting byte m of `word` at bits 8..15, 0x4B at bits 24..31, zeros elsewhere.
+__host__ __device__ constexpr uint32_t byte_sel(int m) { return 0x7404u | ((uint32_t)m << 4); }
+
+// Dot's eight FMA lanes for one 8-weight group (lanes l, l+1 as packed pairs), then
+// QuantizedKAvx2Kernel.HorizontalSum as packed adds: ((a0+a4),(a1+a5)) + ((a2+a6),(a3+a7)), then g0 + g1.
+template <int FMT, int PMAX>
+__device__ __forceinline__ void q_terms_batch_fast(const uint32_t qw[8], float d, uint32_t xbase, int b, int P,
+                                                   int xpos_stride, float (&terms)[PMAX])
+{
+    const float s8 = fmul(d, 0.00390625f);
+    const float c8 = fmul(d, FMT == 0 ? -32896.0f : -32776.0f);  // -d*(2^15 + 128) / -d*(2^15 + 8)
+    const float2 S = make_float2(s8, s8), Cc = make_float2(c8, c8);
+    // Source word of each 4-weight quad q (weights 4q..4q+3).
+    uint32_t src[8];
+    if (FMT == 0) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) src[k] = qw[k] ^ 0x80808080u;
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            src[k] = qw[k] & 0x0F0F0F0Fu;             // weights 4k..4k+3 (low nibbles)
+            src[k + 4] = (qw[k] >> 4) & 0x0F0F0F0Fu;  // weights 16+4k.. (high nibbles)
+        }
+    }
+    float2 w[16];  // w[2q + h]: weights (4q + 2h, 4q + 2h + 1), i.e. Dot lanes (l, l + 1)
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        w[2 * q] = __ffma2_rn(f2pair(src[q], byte_sel(0), byte_sel(1)), S, Cc);
+        w[2 * q + 1] = __ffma2_rn(f2pair(src[q], byte_sel(2), byte_sel(3)), S, Cc);
+    }
+#pragma unroll
+    for (int p = 0; p < PMAX; ++p) {
+        if (p >= P) break;
+        const uint32_t xb = xbase + (uint32_t)(p * xpos_stride);
+        float2 A[4];  // lanes (0,1), (2,3), (4,5), (6,7)
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const float4 x0 = lds128f(xchunk<8>(xb, b, 2 * g));
+            const float4 x1 = lds128f(xchunk<8>(xb, b, 2 * g + 1));
+            const float2 X[4] = {make_float2(x0.x, x0.y), make_float2(x0.z, x0.w), make_float2(x1.x, x1.y),
+                                 make_float2(x1.z, x1.w)};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                A[i] = __ffma2_rn(w[4 * g + i], X[i], g == 0 ? make_float2(0.0f, 0.0f) : A[i]);
+        }
+        const float2 h01 = __fadd2_rn(A[0], A[2]);  // (a0+a4, a1+a5)
+        const float2 h23 = __fadd2_rn(A[1], A[3]);  // (a2+a6, a3+a7)
+        const float2 g01 = __fadd2_rn(h01, h23);    // (h0+h2, h1+h3)
+        terms[p] = fadd(g01.x, g01.y);
+    }
+}
+
 // ---------------------------------------------------------------- Ternary2 block term
 template <int BS, int ORDER>
 __device__ __forceinline__ float t2_term(uint32_t blk, uint32_t xbase, int b, int count)
@@ -290,11 +354,15 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(Geo g)
             if (!abort_flag) {
                 const uint32_t sbase = smem_u32(stage0 + (size_t)s * stage_bytes);
                 const int items = RC * nb;
+                // (row, block) of this thread's first item; later items advance by a fixed (dr, dj).
+                int r = tid / nb, j = tid - (tid / nb) * nb;
+                const int dr = ncompute_threads / nb, dj = ncompute_threads - dr * nb;
+                const uint32_t chunk_ofs = (uint32_t)(c * g.cb * BB);
                 for (int it = tid; it < items; it += ncompute_threads) {
-                    const int r = it / nb, j = it - r * nb;
                     const int b = c * g.cb + j;
-                    const long long gofs = (long long)(r0 + r) * g.row_bytes + (long long)c * g.cb * BB;
-                    const uint32_t blk = sbase + (uint32_t)(r * g.seg_stride) + (uint32_t)(gofs & 15) + (uint32_t)(j * BB);
+                    // Low 4 bits of the segment's global offset = its offset inside the 16-byte-aligned copy.
+                    const uint32_t seg_ofs = ((uint32_t)(r0 + r) * (uint32_t)g.row_bytes + chunk_ofs) & 15u;
+                    const uint32_t blk = sbase + (uint32_t)(r * g.seg_stride) + seg_ofs + (uint32_t)(j * BB);
                     float *dst = D + ((size_t)buf * kMaxRowsPerCta + r) * g.dstride + (size_t)j * g.P;
                     if (FMT <= 1) {
                         // Bytes [0, BB) of a 2-byte aligned block span words 0..NW from the aligned base.
@@ -309,13 +377,22 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(Geo g)
                         for (int k = 0; k < (FMT == 0 ? 8 : 4); ++k) qw[k] = __funnelshift_rc(w[k], w[k + 1], shq);
                         const float d = half_bits_to_float(__funnelshift_rc(w[0], w[1], sh));
                         float terms[PMAX];
-                        q_terms<FMT, ORDER, PMAX>(qw, d, xbase, b, g.P, xpos_stride, terms);
+                        if (ORDER == SATORI_ORDER_BATCH)
+                            q_terms_batch_fast<FMT, PMAX>(qw, d, xbase, b, g.P, xpos_stride, terms);
+                        else
+                            q_terms<FMT, ORDER, PMAX>(qw, d, xbase, b, g.P, xpos_stride, terms);
 #pragma unroll
                         for (int p = 0; p < PMAX; ++p)
                             if (p < g.P) dst[p] = terms[p];
                     } else {
                         const int count = min(BE, g.cols - b * BE);
                         dst[0] = t2_term<BE, ORDER>(blk, xbase, b, count);
+                    }
+                    j += dj;
+                    r += dr;
+                    if (j >= nb) {
+                        j -= nb;
+                        ++r;
                     }
                 }
             }
@@ -390,10 +467,16 @@ GemvPlan plan_gemv(int rows, int cols, int format, int positions, int sm_count, 
     int rc = (rows + grid - 1) / grid;
     if (rc > kMaxRowsPerCta) rc = kMaxRowsPerCta;
     grid = (rows + rc - 1) / rc;
-    // Chunk: ~16 KB of payload per stage, at least 8 blocks when the row has them.
-    int cb = std::max(1, 16384 / std::max(1, rc * BB));
-    cb = std::min(std::max(cb, std::min(8, bpr)), bpr);
-    cb = std::min(cb, 64);
+    // Chunk: a whole number of rounds of the compute threads (rows x blocks <= k * threads) carrying
+    // at least ~12 KB of payload per stage, so every compute thread has the same number of items.
+    const int tc = (8 - (rc + 31) / 32) * 32;
+    int cb = 1;
+    for (int k = 1; k <= 16; ++k) {
+        const int c = std::max(1, (k * tc) / rc);
+        cb = std::min(c, bpr);
+        if (c >= bpr || (size_t)c * rc * BB >= 12288) break;
+    }
+    cb = std::max(1, std::min(cb, 64));
     const int seg_stride = ((cb * BB + 32) + 15) & ~15;
     const int dstride = cb * positions + 1;
     const size_t xbytes = (size_t)positions * bpr * BE * 4;
