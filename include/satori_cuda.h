@@ -131,6 +131,18 @@ SATORI_API int satori_grouped_attention_device(satori_ctx *ctx, const float *q, 
 /* Host-pointer twin (synchronous). */
 SATORI_API int satori_grouped_attention(satori_ctx *ctx, const float *q, const float *keys, const float *values,
                                         int q_heads, int kv_heads, int head_dim, int tokens, float *out);
+/* No counterpart in the reference.  Grouped attention for callers that cannot allocate device
+ * memory (for example a host that has already given the whole GPU to its own memory pool, or a path
+ * that cannot afford cudaMalloc's device-wide synchronisation): the same kernels and result as
+ * satori_grouped_attention_device, with their split-K scratch in a fixed 4 MiB array inside the
+ * library's device image instead of a context allocation.  No context: device pointers and a
+ * cudaStream_t (NULL = legacy default stream) on the current device.  The call allocates nothing; its
+ * first call on a device looks up that array's address, so make that first call before any stream
+ * capture.  Shapes whose partial records exceed 1,048,576 floats are rejected with
+ * SATORI_ERR_ARGUMENT.  Calls share the one array: two calls that overlap on the GPU race. */
+SATORI_API int satori_grouped_attention_noalloc(const float *q, const float *keys, const float *values,
+                                                int q_heads, int kv_heads, int head_dim, int tokens, float *out,
+                                                void *stream);
 /* TransformerOps.RopeHalf (TransformerOps.cs:99-118) on a host vector, in place (FP64 angles). */
 SATORI_API int satori_rope_half(satori_ctx *ctx, float *vector, int n, int head_dim, int position, double base,
                                 int rotary);

@@ -105,6 +105,7 @@ _SIGS = {
     "satori_quantize_q_device": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.c_int, _vp]),
     "satori_grouped_attention_device": (C.c_int, [_vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),
     "satori_grouped_attention": (C.c_int, [_vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),
+    "satori_grouped_attention_noalloc": (C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp]),
     "satori_rope_half": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.c_int, C.c_double, C.c_int]),
     "satori_attn_create": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_double, C.POINTER(_vp)]),
     "satori_attn_append": (C.c_int, [_vp, C.c_int, C.c_int, _vp, _vp, _vp, _vp]),
