@@ -120,6 +120,35 @@ int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int 
     const int per_launch = order == SATORI_ORDER_BATCH ? 8 : 1;
     for (int p0 = 0; p0 < positions; p0 += per_launch) {
         const int np = std::min(per_launch, positions - p0);
+        if (order == SATORI_ORDER_BATCH && np == 1) {
+            // One decode position: the dedicated kernel when the shape qualifies.
+            GemvArgs a = {};
+            a.payload = d_payload;
+            a.rows = rows;
+            a.cols = cols;
+            a.format = format;
+            a.order = order;
+            a.x = dx + (size_t)p0 * cols;
+            a.y = dy + (size_t)p0 * rows;
+            a.positions = 1;
+            a.epilogue = epilogue;
+            a.bias = bias;
+            a.residual = residual;
+            a.err = ctx->d_err;
+            a.use_pdl = use_pdl;
+            DecodePlan dp = plan_gemv_rows(a, ctx->sm_count, ctx->smem_optin);
+            if (dp.ok) {
+                cudaError_t e = launch_gemv_rows(a, dp, stream);
+                if (e != cudaSuccess) return cuda_fail(e, "launch decode MatVec");
+                continue;
+            }
+            dp = plan_gemv_decode(a, ctx->sm_count, ctx->smem_optin);
+            if (dp.ok) {
+                cudaError_t e = launch_gemv_decode(a, dp, stream);
+                if (e != cudaSuccess) return cuda_fail(e, "launch decode MatVec");
+                continue;
+            }
+        }
         GemvPlan plan = plan_gemv(rows, cols, format, np, ctx->sm_count, ctx->smem_optin);
         if (!plan.ok) return set_error(SATORI_ERR_ARGUMENT, "no MatVec plan fits shared memory for %dx%d", rows, cols);
         GemvArgs a = {};
@@ -325,8 +354,10 @@ extern "C" int satori_matrix_execute_device(satori_matrix *m, const float *dx, f
         return set_error(SATORI_ERR_ARGUMENT, "only the batch order takes several positions");
     if (order == SATORI_ORDER_BATCH && m->format > 1)
         return set_error(SATORI_ERR_NOT_SUPPORTED, "ExecuteBatch is defined for Q8_0/Q4_0 only");
+    // Launched with programmatic dependent launch: the kernel streams its weights while the previous
+    // kernel on the stream finishes, and waits for it before reading x or writing y.
     return run_gemv(m->ctx, m->d_payload, m->rows, m->cols, m->format, order, dx, dy, positions, kEpiNone, nullptr,
-                    nullptr, m->ctx->stream, 0);
+                    nullptr, m->ctx->stream, 1);
 }
 
 extern "C" int satori_matrix_read_row(satori_matrix *m, int row, float *out)

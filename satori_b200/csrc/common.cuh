@@ -63,6 +63,19 @@ __device__ __forceinline__ float4 lds128f(uint32_t addr)
     return v;
 }
 
+__device__ __forceinline__ uint2 lds64(uint32_t addr)
+{
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ void sts128f(uint32_t addr, float4 v)
+{
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" :: "r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
 // --------------------------------------------------------------------------- mbarrier + bulk copy
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
 {
@@ -90,15 +103,46 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
     return ok != 0;
 }
 
+// Non-blocking test of a phase (no suspension).
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
 // Bounded wait: returns false (and the caller records a timeout) if the phase never flips.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity)
 {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_test(bar, parity)) return true;
     long long start = clock64();
     while (!mbar_try_wait(bar, parity)) {
         if (clock64() - start > kWaitBudgetCycles) return false;
     }
     return true;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
+
+// 2-D tiled TMA load (unicast, no multicast) of the box at (c0 = inner, c1 = outer) of `map`
+// into shared memory, completing on `bar`.  `map` is the address of a __grid_constant__ kernel
+// parameter; c0 * element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *map, int c0, int c1, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                 :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const void *map)
+{
+    asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 // 1-D bulk copy global -> shared (TMA unicast, no multicast), completing on `bar`.

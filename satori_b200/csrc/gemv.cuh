@@ -35,6 +35,18 @@ struct GemvPlan {
 };
 
 GemvPlan plan_gemv(int rows, int cols, int format, int positions, int sm_count, size_t smem_limit);
+
+// Decode-order MatVec of one position for Q8_0 / Q4_0 with cols % 256 == 0: gemv_rows.cu (up to
+// 8192 columns, kind 1) and gemv_decode.cu (column chunks, any width, kind 2).  A plan function returns
+// ok = 0 for any argument set its kernel does not take.
+struct DecodePlan {
+    int ok, kind, grid, rc, stages, nchunks, rs;
+    size_t smem;
+};
+DecodePlan plan_gemv_rows(const GemvArgs &a, int sm_count, size_t smem_limit);
+cudaError_t launch_gemv_rows(const GemvArgs &a, const DecodePlan &plan, cudaStream_t stream);
+DecodePlan plan_gemv_decode(const GemvArgs &a, int sm_count, size_t smem_limit);
+cudaError_t launch_gemv_decode(const GemvArgs &a, const DecodePlan &plan, cudaStream_t stream);
 cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &plan, cudaStream_t stream);
 int gemv_block_bytes(int format);
 int gemv_block_elems(int format);
