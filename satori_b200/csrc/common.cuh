@@ -114,12 +114,24 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity)
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes (or ~hint_ns pass)
+// instead of spinning, leaving the issue slots to the warps that have work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns) : "memory");
+    return ok != 0;
+}
+
 // Bounded wait: returns false (and the caller records a timeout) if the phase never flips.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity)
 {
     if (mbar_test(bar, parity)) return true;
     long long start = clock64();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity, 100000u)) {
         if (clock64() - start > kWaitBudgetCycles) return false;
     }
     return true;

@@ -164,6 +164,9 @@ __device__ __forceinline__ bool rows_compute(const RowsGeo &g, uint8_t *smem, in
         }
         // Last stage of the fold batch (or of the CTA): this warp's terms of the batch are written.
         if (r0 + g.rs >= kFoldRows || i == nst - 1) {
+            // Every warp, with rows in the batch or not, arrives only once batch fb - kFoldSlots has been
+            // added in: dfull[fb % kFoldSlots] is then in batch fb's phase, never in an earlier batch's.
+            if (!dready && !rows_wait_counter(h.folded, fb - kFoldSlots + 1)) return false;
             __syncwarp();
             if (lane == 0) mbar_arrive(&h.dfull[fb % kFoldSlots]);
         }
