@@ -167,6 +167,9 @@ def events_time(fn, stream, steps: int) -> float:
 MATVEC_SHAPES = [(0, 4096, 4096), (1, 11008, 4096)]
 MATVEC_METRIC = "MatVec payload GB/s (GGUF Q8_0 4096x4096 + Q4_0 11008x4096, decode ExecuteBatch order)"
 MATVEC_WORKLOAD = "configs[1]: GGUF Q8_0 4096x4096 and Q4_0 11008x4096 MatVec"
+# dram__bytes_read.sum + dram__bytes_write.sum per launch, averaged over the two kernels, from one ncu
+# capture of this workload (Q8_0 17,875,712 + Q4_0 25,412,352 bytes; profiles/gemv_rows_matvec_bench.md).
+MATVEC_NCU_TRAFFIC = (17875712 + 25412352) / 2
 
 
 def bench_matvec(args, rank, world, local):
@@ -244,7 +247,8 @@ def bench_matvec(args, rank, world, local):
                    "parallelism": f"replicas x{world} (independent matrices per rank)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": None, "algorithmic_bytes_per_launch": step_bytes / 2},
+                     "traffic": MATVEC_NCU_TRAFFIC, "traffic_source": "profiles/gemv_rows_matvec_bench.md",
+                     "algorithmic_bytes_per_launch": step_bytes / 2},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 2 * 4096 * 4,
                 "d2h_bytes_per_step": (4096 + 11008) * 4},
         "gpu_launches": launches,
