@@ -14,6 +14,8 @@
 // reduced across the warp with a transposed butterfly (9 shuffles instead of 40).  Online softmax
 // state (m, l, acc) is kept per warp, merged per CTA into one partial record, and the records of
 // all splits are merged by a second kernel.
+#include <cuda.h>
+
 #include "attention.cuh"
 #include "common.cuh"
 
@@ -36,6 +38,7 @@ struct AttnParams {
     float scale;
     float *scratch;
     float *out;
+    unsigned *err;
     int use_pdl;
 };
 
@@ -208,6 +211,209 @@ __global__ void __launch_bounds__(kWarps * 32) attn_partial_kernel(AttnParams p)
                     if (VEC4) { lane_d = d >> 2; i_d = d & 3; } else { lane_d = d & 31; i_d = d >> 5; }
                     x = wacc[w][h][i_d * 32 + lane_d];
                 }
+                val = fmaf(x, f, val);
+            }
+        }
+        p.scratch[((long long)split * p.q_heads + h0 + h) * rec_stride + e] = val;
+    }
+    if (p.use_pdl) pdl_launch_dependents();
+}
+
+// Streaming variant for head_dim 128 and groups of up to 8 query heads (every BASELINE shape):
+// a producer warp streams the split's K and V rows of one KV head in 8-token tiles with 3-D TMA
+// loads (unicast) into a ring of 16 shared-memory slots, two per compute warp, so that ~64 KB per
+// SM are in flight; compute warp w takes tiles w, w + 8, ... and runs the same per-token arithmetic
+// as attn_partial_kernel (lane = 4 dims, transposed butterfly, per-warp online softmax), reading K and
+// V from shared memory.  The per-warp states are merged into the same partial records.
+constexpr int kStreamWarps = 8;
+constexpr int kStreamTok = 8;                       // tokens per tile
+constexpr int kStreamSlots = 2 * kStreamWarps;
+constexpr int kStreamTileBytes = kStreamTok * 128 * 4;
+constexpr int kStreamHeader = 384;             // full[16] + empty[16] mbarriers, then the abort flag
+constexpr int kStreamPBytes = kStreamWarps * 8 * kStreamTok * 4;
+constexpr size_t kStreamSmem =
+    128 + kStreamHeader + kStreamPBytes + (size_t)kStreamSlots * 2 * kStreamTileBytes;
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const void *map, int c0, int c1, int c2, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+                 :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2),
+                    "r"(smem_u32(bar))
+                 : "memory");
+}
+
+__global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
+    attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnParams p)
+{
+    constexpr int GMAX = 8, DPL = 4, R = 32 / GMAX;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + kStreamSlots;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStreamSlots);
+    float (*P)[GMAX][kStreamTok] = reinterpret_cast<float (*)[GMAX][kStreamTok]>(smem + kStreamHeader);
+    uint8_t *slots = smem + kStreamHeader + kStreamPBytes;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int split = blockIdx.x;
+    const int kvh = blockIdx.y / p.ngroups, grp = blockIdx.y % p.ngroups;
+    const int h0 = kvh * p.group + grp * GMAX;
+    const int gc = min(GMAX, p.group - grp * GMAX);
+    const int hd = 128;
+    const int hl = lane / R;
+
+    if (tid == 0) {
+        *abort_flag = 0;
+        for (int s = 0; s < kStreamSlots; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (p.use_pdl) pdl_wait();   // the token count and the newest K/V row come from earlier kernels
+    const int T = p.tokens_dev ? *p.tokens_dev : p.tokens;
+    const int t0 = (int)(((long long)T * split) / p.nsplit);
+    const int t1 = (int)(((long long)T * (split + 1)) / p.nsplit);
+    const int nst = (t1 - t0 + kStreamTok - 1) / kStreamTok;
+
+    float acc[GMAX][DPL];
+#pragma unroll
+    for (int h = 0; h < GMAX; ++h)
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[h][i] = 0.0f;
+    float m_my = -INFINITY, l_my = 0.0f;
+
+    if (warp == kStreamWarps) {
+        if (lane == 0) {
+            auto issue = [&](int k) {
+                const int s = k % kStreamSlots;
+                uint8_t *dst = slots + (size_t)s * 2 * kStreamTileBytes;
+                mbar_expect_tx(&full[s], 2u * kStreamTileBytes);
+                tma_load_3d(dst, &kmap, 0, kvh, t0 + k * kStreamTok, &full[s]);
+                tma_load_3d(dst + kStreamTileBytes, &vmap, 0, kvh, t0 + k * kStreamTok, &full[s]);
+            };
+            prefetch_tensormap(&kmap);
+            prefetch_tensormap(&vmap);
+            const int first = min(kStreamSlots, nst);
+            for (int k = 0; k < first; ++k) issue(k);
+            int k = 0;
+            for (; k + kStreamSlots < nst; ++k) {
+                if (*abort_flag || !mbar_wait_bounded(&empty[k % kStreamSlots], (uint32_t)((k / kStreamSlots) & 1))) {
+                    if (p.err) atomicOr(p.err, kDevErrTimeout);
+                    *abort_flag = 1;
+                    break;
+                }
+                issue(k + kStreamSlots);
+            }
+            // Every copy issued lands before the CTA's shared memory goes away.
+            const int last = min(k + kStreamSlots, nst) - 1;
+            for (int j = max(0, last - kStreamSlots + 1); j <= last; ++j)
+                mbar_wait_bounded(&full[j % kStreamSlots], (uint32_t)((j / kStreamSlots) & 1));
+        }
+    } else {
+        float qr[GMAX][DPL];
+#pragma unroll
+        for (int h = 0; h < GMAX; ++h)
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) qr[h][i] = h < gc ? p.q[(h0 + h) * hd + 4 * lane + i] : 0.0f;
+        for (int k = warp; k < nst; k += kStreamWarps) {
+            const int s = k % kStreamSlots;
+            if (*abort_flag) break;
+            if (!mbar_wait_bounded(&full[s], (uint32_t)((k / kStreamSlots) & 1))) {
+                if (p.err) atomicOr(p.err, kDevErrTimeout);
+                *abort_flag = 1;
+                break;
+            }
+            const uint32_t kt = smem_u32(slots + (size_t)s * 2 * kStreamTileBytes) + 16u * lane;
+            const uint32_t vt = kt + kStreamTileBytes;
+            const int tb = t0 + k * kStreamTok;
+            const int nt = min(kStreamTok, t1 - tb);
+            float sc[kStreamTok];
+#pragma unroll
+            for (int j = 0; j < kStreamTok; ++j) {
+                if (j < nt) {
+                    const float4 t4 = lds128f(kt + 512u * j);
+                    const float kr[DPL] = {t4.x, t4.y, t4.z, t4.w};
+                    float v[8];
+#pragma unroll
+                    for (int h = 0; h < 8; ++h) {
+                        float a = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < DPL; ++i) a = fmaf(qr[h][i], kr[i], a);
+                        v[h] = a;
+                    }
+                    sc[j] = transpose_reduce<GMAX>(v, lane) * p.scale;
+                } else {
+                    sc[j] = -INFINITY;
+                }
+            }
+            float mb = sc[0];
+#pragma unroll
+            for (int j = 1; j < kStreamTok; ++j) mb = fmaxf(mb, sc[j]);
+            const float m_new = fmaxf(m_my, mb);
+            const float alpha = m_my == -INFINITY ? 0.0f : expf(m_my - m_new);
+            float lsum = 0.0f;
+#pragma unroll
+            for (int j = 0; j < kStreamTok; ++j) {
+                const float pj = j < nt ? expf(sc[j] - m_new) : 0.0f;
+                lsum += pj;
+                if ((j % R) == (lane % R)) P[warp][hl][j] = pj;
+            }
+            l_my = l_my * alpha + lsum;
+            m_my = m_new;
+            float alpha_h[GMAX];
+#pragma unroll
+            for (int h = 0; h < GMAX; ++h) alpha_h[h] = __shfl_sync(0xFFFFFFFFu, alpha, h * R);
+#pragma unroll
+            for (int h = 0; h < GMAX; ++h)
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) acc[h][i] *= alpha_h[h];
+            __syncwarp();
+            for (int j = 0; j < nt; ++j) {
+                const float4 t4 = lds128f(vt + 512u * j);
+                const float vr[DPL] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+                for (int h = 0; h < GMAX; ++h) {
+                    const float pj = P[warp][h][j];
+#pragma unroll
+                    for (int i = 0; i < DPL; ++i) acc[h][i] = fmaf(pj, vr[i], acc[h][i]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);   // the producer may refill this slot
+        }
+    }
+    __syncthreads();   // every tile consumed: the slots now hold the per-warp states
+
+    float *wm = reinterpret_cast<float *>(slots);                    // [kStreamWarps][GMAX]
+    float *wl = wm + kStreamWarps * GMAX;                             // [kStreamWarps][GMAX]
+    float *wacc = wl + kStreamWarps * GMAX;                           // [kStreamWarps][GMAX][128]
+    if (warp < kStreamWarps) {
+        if (lane % R == 0) {
+            wm[warp * GMAX + hl] = m_my;
+            wl[warp * GMAX + hl] = l_my;
+        }
+#pragma unroll
+        for (int h = 0; h < GMAX; ++h)
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) wacc[(warp * GMAX + h) * hd + 4 * lane + i] = acc[h][i];
+    }
+    __syncthreads();
+    const int rec_stride = hd + 2;
+    for (int idx = tid; idx < gc * rec_stride; idx += blockDim.x) {
+        const int h = idx / rec_stride, e = idx - h * rec_stride;
+        float m = wm[h];
+#pragma unroll
+        for (int w = 1; w < kStreamWarps; ++w) m = fmaxf(m, wm[w * GMAX + h]);
+        float val = 0.0f;
+        if (e == 0) {
+            val = m;
+        } else {
+            for (int w = 0; w < kStreamWarps; ++w) {
+                const float mw = wm[w * GMAX + h];
+                const float f = mw == -INFINITY ? 0.0f : expf(mw - m);
+                const float x = e == 1 ? wl[w * GMAX + h] : wacc[(w * GMAX + h) * hd + (e - 2)];
                 val = fmaf(x, f, val);
             }
         }
@@ -432,6 +638,74 @@ size_t attn_scratch_floats(int q_heads, int kv_heads, int head_dim, int max_toke
     return (size_t)attn_splits(q_heads, kv_heads, head_dim, max_tokens, sm_count) * q_heads * (head_dim + 2);
 }
 
+namespace {
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn attn_encode_fn()
+{
+    static EncodeTiledFn fn = [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(f);
+    }();
+    return fn;
+}
+
+// K or V cache of one layer as a 3-D FP32 tensor [tokens][kv_heads][128], boxes of 8 tokens x 1 head.
+bool encode_kv_map(CUtensorMap *map, const float *base, int kv_heads, int tokens)
+{
+    EncodeTiledFn enc = attn_encode_fn();
+    if (!enc || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+    const cuuint64_t dims[3] = {128, (cuuint64_t)kv_heads, (cuuint64_t)tokens};
+    const cuuint64_t strides[2] = {128 * 4, (cuuint64_t)kv_heads * 128 * 4};
+    const cuuint32_t box[3] = {128, 1, (cuuint32_t)kStreamTok};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The streaming kernel takes head_dim 128 with groups of 5..8 (or more) query heads per KV head.
+// Returns false (nothing launched) when the shape or pointers do not qualify.
+bool launch_stream(const AttnArgs &a, AttnParams &p, int gmax, int sm_count, cudaStream_t stream, cudaError_t *err)
+{
+    if (a.head_dim != 128 || gmax != 8) return false;
+    const int units = a.kv_heads * p.ngroups;
+    const int cap = std::max(a.max_tokens, a.tokens);
+    CUtensorMap kmap, vmap;
+    if (!encode_kv_map(&kmap, a.keys, a.kv_heads, cap) || !encode_kv_map(&vmap, a.values, a.kv_heads, cap)) return false;
+    // About one CTA per SM (each keeps ~64 KB in flight); never more splits than the scratch holds.
+    p.nsplit = std::max(1, std::min(p.nsplit, (sm_count + units - 1) / units));
+    static bool configured = false;
+    if (!configured) {
+        const cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)kStreamSmem);
+        if (e != cudaSuccess) {
+            *err = e;
+            return true;
+        }
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.nsplit, units);
+    cfg.blockDim = dim3((kStreamWarps + 1) * 32);
+    cfg.dynamicSmemBytes = kStreamSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = p.use_pdl ? 1 : 0;
+    *err = cudaLaunchKernelEx(&cfg, attn_stream_kernel, kmap, vmap, p);
+    return true;
+}
+}  // namespace
+
 cudaError_t launch_attention(const AttnArgs &a, int sm_count, cudaStream_t stream)
 {
     if (a.head_dim <= 0 || a.head_dim > 256 || a.q_heads % a.kv_heads != 0) return cudaErrorInvalidValue;
@@ -452,10 +726,13 @@ cudaError_t launch_attention(const AttnArgs &a, int sm_count, cudaStream_t strea
     p.scratch = a.scratch;
     p.out = a.out;
     p.use_pdl = a.use_pdl;
-    const dim3 grid(p.nsplit, a.kv_heads * p.ngroups);
+    p.err = a.err;
     cudaError_t e;
-    if (a.head_dim == 128) e = launch_partial_g<4, true>(p, gmax, grid, stream);
-    else e = launch_partial_g<8, false>(p, gmax, grid, stream);
+    if (!launch_stream(a, p, gmax, sm_count, stream, &e)) {
+        const dim3 grid(p.nsplit, a.kv_heads * p.ngroups);
+        if (a.head_dim == 128) e = launch_partial_g<4, true>(p, gmax, grid, stream);
+        else e = launch_partial_g<8, false>(p, gmax, grid, stream);
+    }
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.q_heads);
