@@ -419,7 +419,11 @@ def bench_decode(args, rank, world, local, spec):
     context = args.prompt + args.decode + 8
     tensors = device_model(ctx, spec, seed=31)
     torch.cuda.synchronize()
-    sess = sat.CudaDenseSession(spec, tensors, context, ctx=ctx)
+    if world == 1:
+        sess = sat.CudaDenseSession(spec, tensors, context, ctx=ctx)
+    else:
+        sess = sat.CudaDenseSession(spec, tensors, context, ctx=ctx, rank=rank, world=world,
+                                    nccl_id=sat.broadcast_nccl_id())
     del tensors
     torch.cuda.empty_cache()
     prompt = np.random.default_rng(4).integers(0, spec.vocab, args.prompt).astype(np.int32)
@@ -439,14 +443,16 @@ def bench_decode(args, rank, world, local, spec):
     tps = args.decode / (ms / 1e3)
     wbytes = spec.weight_bytes(include_embedding_table=False) + spec.hidden // 32 * 34
     kv_avg = 2 * spec.layers * spec.kv_width * 4 * (args.prompt + args.decode / 2)
-    achieved = (wbytes + kv_avg) / (ms / 1e3 / args.decode) / GB
+    # Per GPU: a 1/world row share of every matrix and the KV heads of this rank's query heads.
+    achieved = (wbytes + kv_avg) / world / (ms / 1e3 / args.decode) / GB
     peak, peak_kind = _peaks()
     return {"metric": f"decode tokens/s ({spec.name})", "value": round(tps, 2), "unit": "tokens/s",
             "n_gpus": world, "steps": args.decode, "warmup": args.prompt, "ms_per_step": round(ms / args.decode, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "quantized weights, f32 activations", "data": "synthetic seeded weights, random prompt",
             "config": {"workload": spec.name, "prompt": args.prompt, "decode": args.decode,
-                       "parallelism": "single GPU" if world == 1 else f"tp{world}"},
+                       "parallelism": "single GPU" if world == 1 else
+                       f"tp{world}: row-sharded projections, query-head-sharded attention, NCCL all-gathers"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
                          "algorithmic_bytes_per_launch": wbytes + kv_avg},

@@ -181,11 +181,18 @@ typedef struct satori_model_desc {
  * (embed, every layer, final norm, logits, greedy argmax) run on the device. */
 SATORI_API int satori_session_create(satori_ctx *ctx, const satori_model_desc *desc, int context,
                                      satori_session **out);
-/* Multi-GPU variant: this process is `rank` of `world` (one process per GPU).  Projections are
- * row-sharded and attention is KV-head sharded; activations are all-gathered over NCCL.
- * `nccl_unique_id` is the 128-byte ncclUniqueId every rank received from rank 0. */
+/* Multi-GPU variant (no counterpart in the reference, which runs on one CPU): this process is `rank`
+ * of `world`, one process per GPU, all ranks calling together.  Every projection is row-sharded (a
+ * row's FP32 chain stays on one GPU, so logits equal the single-GPU session's); attention is sharded
+ * by query heads, each rank caching only the KV heads its heads read; the context, the residual
+ * after attn_output / ffn_down, the SwiGLU activations and the logits are all-gathered with NCCL
+ * inside the step's CUDA graph.  hidden, ffn and vocab must be multiples of `world`
+ * (SATORI_ERR_NOT_SUPPORTED otherwise).  Every rank passes the full tensor table and uploads only
+ * its rows.  `nccl_unique_id` is the 128-byte id from satori_nccl_unique_id on rank 0.  world = 1 is
+ * satori_session_create. */
 SATORI_API int satori_session_create_sharded(satori_ctx *ctx, const satori_model_desc *desc, int context, int rank,
                                              int world, const void *nccl_unique_id, satori_session **out);
+/* ncclGetUniqueId through the NCCL library loaded at run time (128 bytes into out128). */
 SATORI_API int satori_nccl_unique_id(void *out128);
 /* DenseSession.Append (DenseSession.cs:111-131) + GreedyTokenSelector.Select
  * (src/Satori.Core/GreedyTokenSelector.cs:6-16): logits (host, may be NULL) and argmax (may be NULL). */

@@ -59,7 +59,7 @@ def build(force: bool = False, verbose: bool = False, extra=()) -> str:
         return LIB_PATH
     os.makedirs(BUILD_DIR, exist_ok=True)
     tmp = LIB_PATH + ".tmp"
-    cmd = [_nvcc(), *NVCC_FLAGS, *extra, "-o", tmp, *sources(), "-lcuda"]
+    cmd = [_nvcc(), *NVCC_FLAGS, *extra, "-o", tmp, *sources(), "-lcuda", "-ldl"]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

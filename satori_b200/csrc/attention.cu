@@ -32,6 +32,7 @@ constexpr int kTokBlock = 32;
 struct AttnParams {
     const float *q, *keys, *values;
     int q_heads, kv_heads, head_dim, group, ngroups;
+    int kv_stride;   // floats between consecutive tokens' K (or V) rows
     int tokens;
     const int *tokens_dev;
     int nsplit;
@@ -95,7 +96,7 @@ __global__ void __launch_bounds__(kWarps * 32) attn_partial_kernel(AttnParams p)
     const int h0 = kvh * p.group + grp * GMAX;
     const int gc = min(GMAX, p.group - grp * GMAX);
     const int hd = p.head_dim;
-    const int kvw = p.kv_heads * hd;
+    const int kvw = p.kv_stride;
     const int hl = lane / R;
 
     if (p.use_pdl) pdl_wait();
@@ -425,7 +426,7 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
 // FP64 recompute of one head (the reference's arithmetic), used when FP32 scores overflowed.
 __device__ void head_fp64(const AttnParams &p, int head, int T, double *sbuf, float *out)
 {
-    const int hd = p.head_dim, kvw = p.kv_heads * hd;
+    const int hd = p.head_dim, kvw = p.kv_stride;
     const int kvh = head / p.group;
     const float *q = p.q + (long long)head * hd;
     const double scale = 1.0 / sqrt((double)hd);
@@ -656,13 +657,14 @@ EncodeTiledFn attn_encode_fn()
     return fn;
 }
 
-// K or V cache of one layer as a 3-D FP32 tensor [tokens][kv_heads][128], boxes of 8 tokens x 1 head.
-bool encode_kv_map(CUtensorMap *map, const float *base, int kv_heads, int tokens)
+// K or V cache of one layer as a 3-D FP32 tensor [tokens][kv_heads][128] (token rows kv_stride floats
+// apart), boxes of 8 tokens x 1 head.
+bool encode_kv_map(CUtensorMap *map, const float *base, int kv_heads, int kv_stride, int tokens)
 {
     EncodeTiledFn enc = attn_encode_fn();
-    if (!enc || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+    if (!enc || (reinterpret_cast<uintptr_t>(base) & 15) || (kv_stride % 4) != 0) return false;
     const cuuint64_t dims[3] = {128, (cuuint64_t)kv_heads, (cuuint64_t)tokens};
-    const cuuint64_t strides[2] = {128 * 4, (cuuint64_t)kv_heads * 128 * 4};
+    const cuuint64_t strides[2] = {128 * 4, (cuuint64_t)kv_stride * 4};
     const cuuint32_t box[3] = {128, 1, (cuuint32_t)kStreamTok};
     const cuuint32_t estr[3] = {1, 1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box, estr,
@@ -678,7 +680,9 @@ bool launch_stream(const AttnArgs &a, AttnParams &p, int gmax, int sm_count, cud
     const int units = a.kv_heads * p.ngroups;
     const int cap = std::max(a.max_tokens, a.tokens);
     CUtensorMap kmap, vmap;
-    if (!encode_kv_map(&kmap, a.keys, a.kv_heads, cap) || !encode_kv_map(&vmap, a.values, a.kv_heads, cap)) return false;
+    if (!encode_kv_map(&kmap, a.keys, a.kv_heads, p.kv_stride, cap) ||
+        !encode_kv_map(&vmap, a.values, a.kv_heads, p.kv_stride, cap))
+        return false;
     // About one CTA per SM (each keeps ~64 KB in flight); never more splits than the scratch holds.
     p.nsplit = std::max(1, std::min(p.nsplit, (sm_count + units - 1) / units));
     static bool configured = false;
@@ -717,6 +721,7 @@ cudaError_t launch_attention(const AttnArgs &a, int sm_count, cudaStream_t strea
     p.kv_heads = a.kv_heads;
     p.head_dim = a.head_dim;
     p.group = a.q_heads / a.kv_heads;
+    p.kv_stride = a.kv_stride > 0 ? a.kv_stride : a.kv_heads * a.head_dim;
     const int gmax = gmax_for(p.group);
     p.ngroups = (p.group + gmax - 1) / gmax;
     p.tokens = a.tokens;

@@ -11,6 +11,7 @@ struct AttnArgs {
     const float *keys;    // token-major [tokens][kv_heads * head_dim]
     const float *values;
     int q_heads, kv_heads, head_dim;
+    int kv_stride;        // floats between consecutive tokens' rows; 0 = kv_heads * head_dim
     int tokens;           // used when tokens_dev == nullptr
     const int *tokens_dev;  // device-side token count (decode graphs: position + 1)
     int max_tokens;       // upper bound of tokens (sizes the split plan)

@@ -17,6 +17,7 @@
 
 #include <string.h>
 
+#include <algorithm>
 #include <string>
 #include <vector>
 
@@ -42,8 +43,10 @@ const satori_tensor *find_tensor(const satori_model_desc *d, const std::string &
     return nullptr;
 }
 
+// Uploads rows [r0, r1) of the named matrix (all rows when r1 <= r0).  Rows are contiguous in the
+// GGUF payload, so a row slice is one contiguous byte range.
 int fetch_matrix(satori_session *s, const satori_model_desc *d, const std::string &name, int rows, int cols,
-                 DevMatrix *out)
+                 DevMatrix *out, int r0 = 0, int r1 = 0)
 {
     const satori_tensor *t = find_tensor(d, name);
     if (!t) return set_error(SATORI_ERR_ARGUMENT, "missing tensor %s", name.c_str());
@@ -53,19 +56,26 @@ int fetch_matrix(satori_session *s, const satori_model_desc *d, const std::strin
     if (t->bytes != payload_bytes(rows, cols, t->format))
         return set_error(SATORI_ERR_ARGUMENT, "tensor %s has %zu bytes, expected %zu", name.c_str(), t->bytes,
                          payload_bytes(rows, cols, t->format));
+    if (r1 <= r0) {
+        r0 = 0;
+        r1 = rows;
+    }
+    const size_t row_bytes = payload_bytes(1, cols, t->format);
     uint8_t *dp = nullptr;
-    TRY(upload_payload(s->ctx, (const uint8_t *)t->data, false, t->bytes, rows, cols, t->format, &dp));
+    TRY(upload_payload(s->ctx, (const uint8_t *)t->data + (size_t)r0 * row_bytes, false, (size_t)(r1 - r0) * row_bytes,
+                       r1 - r0, cols, t->format, &dp));
     s->allocations.push_back(dp);
     out->payload = dp;
-    out->rows = rows;
+    out->rows = r1 - r0;
     out->cols = cols;
     out->format = t->format;
-    s->weight_bytes += t->bytes;
+    s->weight_bytes += (size_t)(r1 - r0) * row_bytes;
     return SATORI_OK;
 }
 
+// Uploads elements [e0, e0 + count) of the named float vector of length n (all of it when count <= 0).
 int fetch_vector(satori_session *s, const satori_model_desc *d, const std::string &name, int n, float **out,
-                 bool optional = false)
+                 bool optional = false, int e0 = 0, int count = 0)
 {
     const satori_tensor *t = find_tensor(d, name);
     if (!t) {
@@ -77,10 +87,14 @@ int fetch_vector(satori_session *s, const satori_model_desc *d, const std::strin
     }
     if (t->format != -1 || t->rows != n || t->bytes != (size_t)n * 4)
         return set_error(SATORI_ERR_ARGUMENT, "tensor %s must be %d float32 values", name.c_str(), n);
+    if (count <= 0) {
+        e0 = 0;
+        count = n;
+    }
     float *dv = nullptr;
-    TRYCUDA(cudaMalloc(&dv, (size_t)n * 4), "upload vector");
+    TRYCUDA(cudaMalloc(&dv, (size_t)count * 4), "upload vector");
     s->allocations.push_back(dv);
-    TRYCUDA(cudaMemcpy(dv, t->data, (size_t)n * 4, cudaMemcpyDefault), "upload vector");
+    TRYCUDA(cudaMemcpy(dv, (const float *)t->data + e0, (size_t)count * 4, cudaMemcpyDefault), "upload vector");
     *out = dv;
     return SATORI_OK;
 }
@@ -96,11 +110,15 @@ int dalloc(satori_session *s, T **p, size_t n)
 
 }  // namespace
 
-// Enqueues one decode step on `st` (captured into the graph).
+// Enqueues one decode step on `st` (captured into the graph).  A sharded rank computes its rows of
+// every projection and its query heads' attention, and all-gathers each result the next operator
+// needs in full (context, residual after attn_output and after ffn_down, SwiGLU activations, logits).
 static int enqueue_step(satori_session *s, cudaStream_t st)
 {
     const int pdl = s->use_pdl;
-    const int H = s->hidden, F = s->ffn, qw = s->q_width, kvw = s->kv_width;
+    const int H = s->hidden, qw = s->q_width, hd = s->head_dim;
+    const int group = s->q_heads / s->kv_heads;
+    const int nq = s->qb - s->qa, nkv = s->kb - s->ka;
     TRYCUDA(launch_embed(s->embd.payload, H, s->d_token, s->d_pos, s->d_tokens, s->d_hidden, st, pdl), "embed");
     for (int l = 0; l < s->layers; ++l) {
         const Layer &L = s->layer[l];
@@ -112,52 +130,74 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
         TRY(run_gemv(s->ctx, L.v.payload, L.v.rows, H, L.v.format, SATORI_ORDER_BATCH, s->d_normed, s->d_v, 1,
                      L.v_bias ? kEpiBias : kEpiNone, L.v_bias, nullptr, st, pdl));
         if (L.q_norm) {
-            TRYCUDA(launch_rmsnorm_heads(s->d_q, qw, L.q_norm, s->eps, s->head_dim, st, pdl), "q norm");
-            TRYCUDA(launch_rmsnorm_heads(s->d_k, kvw, L.k_norm, s->eps, s->head_dim, st, pdl), "k norm");
+            TRYCUDA(launch_rmsnorm_heads(s->d_q, s->q_local, L.q_norm, s->eps, hd, st, pdl), "q norm");
+            TRYCUDA(launch_rmsnorm_heads(s->d_k, s->kv_local, L.k_norm, s->eps, hd, st, pdl), "k norm");
         }
         RopeAppendArgs r = {};
         r.q = s->d_q;
         r.k = s->d_k;
         r.v = s->d_v;
         r.q_out = s->d_qrot;
-        r.k_cache = s->d_kcache + (size_t)l * s->context * kvw;
-        r.v_cache = s->d_vcache + (size_t)l * s->context * kvw;
-        r.q_heads = s->q_heads;
-        r.kv_heads = s->kv_heads;
-        r.head_dim = s->head_dim;
-        r.rotary = s->head_dim;
+        r.k_cache = s->d_kcache + (size_t)l * s->context * s->kv_local;
+        r.v_cache = s->d_vcache + (size_t)l * s->context * s->kv_local;
+        r.q_heads = nq;
+        r.kv_heads = nkv;
+        r.head_dim = hd;
+        r.rotary = hd;
         r.base = s->rope_base;
         r.position_dev = s->d_pos;
         r.use_pdl = pdl;
         TRYCUDA(launch_rope_append(r, st), "rope/append");
-        AttnArgs a = {};
-        a.q = s->d_qrot;
-        a.keys = r.k_cache;
-        a.values = r.v_cache;
-        a.q_heads = s->q_heads;
-        a.kv_heads = s->kv_heads;
-        a.head_dim = s->head_dim;
-        a.tokens_dev = s->d_tokens;
-        a.max_tokens = s->context;
-        a.out = s->d_ctx;
-        a.scratch = s->d_attn_scratch;
-        a.err = s->ctx->d_err;
-        a.use_pdl = pdl;
-        TRYCUDA(launch_attention(a, s->ctx->sm_count, st), "attention");
-        TRY(run_gemv(s->ctx, L.o.payload, H, qw, L.o.format, SATORI_ORDER_BATCH, s->d_ctx, s->d_proj, 1, kEpiResidual,
-                     nullptr, s->d_hidden, st, pdl));
+        float *ctx_out = s->qmax ? s->d_ctx_pad + (size_t)s->rank * s->qmax * hd : s->d_ctx + (size_t)s->qa * hd;
+        // One launch when this rank's query heads are whole groups; otherwise one per KV head touched.
+        const bool whole = s->qa % group == 0 && s->qb % group == 0;
+        for (int g = whole ? s->ka : s->ka; g < (whole ? s->ka + 1 : s->kb); ++g) {
+            const int qs = whole ? s->qa : std::max(s->qa, g * group);
+            const int qe = whole ? s->qb : std::min(s->qb, (g + 1) * group);
+            const int kg = whole ? s->ka : g;
+            AttnArgs a = {};
+            a.q = s->d_qrot + (size_t)(qs - s->qa) * hd;
+            a.keys = r.k_cache + (size_t)(kg - s->ka) * hd;
+            a.values = r.v_cache + (size_t)(kg - s->ka) * hd;
+            a.q_heads = qe - qs;
+            a.kv_heads = whole ? nkv : 1;
+            a.head_dim = hd;
+            a.kv_stride = s->kv_local;
+            a.tokens_dev = s->d_tokens;
+            a.max_tokens = s->context;
+            a.out = ctx_out + (size_t)(qs - s->qa) * hd;
+            a.scratch = s->d_attn_scratch;
+            a.err = s->ctx->d_err;
+            a.use_pdl = pdl;
+            TRYCUDA(launch_attention(a, s->ctx->sm_count, st), "attention");
+        }
+        if (s->world > 1) {
+            if (s->qmax) {
+                TRY(session_allgather(s, s->d_ctx_pad, (size_t)s->qmax * hd, st));
+                TRYCUDA(launch_ctx_compact(s->d_ctx_pad, s->d_ctx, s->world, s->q_heads, hd, s->qmax, st), "ctx");
+            } else {
+                TRY(session_allgather(s, s->d_ctx, (size_t)s->q_local, st));
+            }
+        }
+        TRY(run_gemv(s->ctx, L.o.payload, s->h1 - s->h0, qw, L.o.format, SATORI_ORDER_BATCH, s->d_ctx,
+                     s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl));
+        TRY(session_allgather(s, s->d_hidden, (size_t)(s->h1 - s->h0), st));
         TRYCUDA(launch_rmsnorm(s->d_hidden, L.ffn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
-        TRY(run_gemv(s->ctx, L.gate.payload, F, H, L.gate.format, SATORI_ORDER_BATCH, s->d_normed, s->d_gate, 1,
+        const int nf = s->f1 - s->f0;
+        TRY(run_gemv(s->ctx, L.gate.payload, nf, H, L.gate.format, SATORI_ORDER_BATCH, s->d_normed, s->d_gate, 1,
                      kEpiNone, nullptr, nullptr, st, pdl));
-        TRY(run_gemv(s->ctx, L.up.payload, F, H, L.up.format, SATORI_ORDER_BATCH, s->d_normed, s->d_up, 1, kEpiNone,
+        TRY(run_gemv(s->ctx, L.up.payload, nf, H, L.up.format, SATORI_ORDER_BATCH, s->d_normed, s->d_up, 1, kEpiNone,
                      nullptr, nullptr, st, pdl));
-        TRYCUDA(launch_swiglu(s->d_gate, s->d_up, F, s->d_act, st, pdl), "swiglu");
-        TRY(run_gemv(s->ctx, L.down.payload, H, F, L.down.format, SATORI_ORDER_BATCH, s->d_act, s->d_proj, 1,
-                     kEpiResidual, nullptr, s->d_hidden, st, pdl));
+        TRYCUDA(launch_swiglu(s->d_gate, s->d_up, nf, s->d_act + s->f0, st, pdl), "swiglu");
+        TRY(session_allgather(s, s->d_act, (size_t)nf, st));
+        TRY(run_gemv(s->ctx, L.down.payload, s->h1 - s->h0, s->ffn, L.down.format, SATORI_ORDER_BATCH, s->d_act,
+                     s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl));
+        TRY(session_allgather(s, s->d_hidden, (size_t)(s->h1 - s->h0), st));
     }
     TRYCUDA(launch_rmsnorm(s->d_hidden, s->output_norm, H, s->eps, s->d_final, st, pdl), "final norm");
-    TRY(run_gemv(s->ctx, s->output.payload, s->vocab, H, s->output.format, SATORI_ORDER_BATCH, s->d_final, s->d_logits,
-                 1, kEpiNone, nullptr, nullptr, st, pdl));
+    TRY(run_gemv(s->ctx, s->output.payload, s->v1 - s->v0, H, s->output.format, SATORI_ORDER_BATCH, s->d_final,
+                 s->d_logits + s->v0, 1, kEpiNone, nullptr, nullptr, st, pdl));
+    TRY(session_allgather(s, s->d_logits, (size_t)(s->v1 - s->v0), st));
     TRYCUDA(launch_argmax_advance(s->d_logits, s->vocab, s->d_argmax, s->d_nonfinite, s->d_pos, s->d_token, st, pdl),
             "argmax");
     return SATORI_OK;
@@ -190,16 +230,17 @@ static int session_upload(satori_session *s, const satori_model_desc *d)
         const std::string p = "blk." + std::to_string(l) + ".";
         TRY(fetch_vector(s, d, p + "attn_norm.weight", H, &L.attn_norm));
         TRY(fetch_vector(s, d, p + "ffn_norm.weight", H, &L.ffn_norm));
-        TRY(fetch_matrix(s, d, p + "attn_q.weight", s->q_width, H, &L.q));
-        TRY(fetch_matrix(s, d, p + "attn_k.weight", s->kv_width, H, &L.k));
-        TRY(fetch_matrix(s, d, p + "attn_v.weight", s->kv_width, H, &L.v));
-        TRY(fetch_matrix(s, d, p + "attn_output.weight", H, s->q_width, &L.o));
-        TRY(fetch_matrix(s, d, p + "ffn_gate.weight", F, H, &L.gate));
-        TRY(fetch_matrix(s, d, p + "ffn_up.weight", F, H, &L.up));
-        TRY(fetch_matrix(s, d, p + "ffn_down.weight", H, F, &L.down));
-        TRY(fetch_vector(s, d, p + "attn_q.bias", s->q_width, &L.q_bias, true));
-        TRY(fetch_vector(s, d, p + "attn_k.bias", s->kv_width, &L.k_bias, true));
-        TRY(fetch_vector(s, d, p + "attn_v.bias", s->kv_width, &L.v_bias, true));
+        const int hd = s->head_dim;
+        TRY(fetch_matrix(s, d, p + "attn_q.weight", s->q_width, H, &L.q, s->qa * hd, s->qb * hd));
+        TRY(fetch_matrix(s, d, p + "attn_k.weight", s->kv_width, H, &L.k, s->ka * hd, s->kb * hd));
+        TRY(fetch_matrix(s, d, p + "attn_v.weight", s->kv_width, H, &L.v, s->ka * hd, s->kb * hd));
+        TRY(fetch_matrix(s, d, p + "attn_output.weight", H, s->q_width, &L.o, s->h0, s->h1));
+        TRY(fetch_matrix(s, d, p + "ffn_gate.weight", F, H, &L.gate, s->f0, s->f1));
+        TRY(fetch_matrix(s, d, p + "ffn_up.weight", F, H, &L.up, s->f0, s->f1));
+        TRY(fetch_matrix(s, d, p + "ffn_down.weight", H, F, &L.down, s->h0, s->h1));
+        TRY(fetch_vector(s, d, p + "attn_q.bias", s->q_width, &L.q_bias, true, s->qa * hd, s->q_local));
+        TRY(fetch_vector(s, d, p + "attn_k.bias", s->kv_width, &L.k_bias, true, s->ka * hd, s->kv_local));
+        TRY(fetch_vector(s, d, p + "attn_v.bias", s->kv_width, &L.v_bias, true, s->ka * hd, s->kv_local));
         // Qwen2 carries all three biases or none; a partial set is rejected.
         if (!!L.q_bias != !!L.k_bias || !!L.q_bias != !!L.v_bias)
             return set_error(SATORI_ERR_ARGUMENT, "layer %d has a partial q/k/v bias set", l);
@@ -215,27 +256,29 @@ static int session_upload(satori_session *s, const satori_model_desc *d)
     if (s->embd.format != SATORI_Q8_0)
         return set_error(SATORI_ERR_NOT_SUPPORTED, "embedding rows must be Q8_0");
     TRY(fetch_vector(s, d, "output_norm.weight", H, &s->output_norm));
-    if (d->tied_embeddings) s->output = s->embd;
-    else TRY(fetch_matrix(s, d, "output.weight", d->vocab, H, &s->output));
+    if (d->tied_embeddings && s->world == 1) s->output = s->embd;
+    else if (d->tied_embeddings) TRY(fetch_matrix(s, d, "token_embd.weight", d->vocab, H, &s->output, s->v0, s->v1));
+    else TRY(fetch_matrix(s, d, "output.weight", d->vocab, H, &s->output, s->v0, s->v1));
     return SATORI_OK;
 }
 
 int session_alloc_state(satori_session *s)
 {
-    const size_t kv = (size_t)s->layers * s->context * s->kv_width;
+    const size_t kv = (size_t)s->layers * s->context * s->kv_local;
     TRY(dalloc(s, &s->d_kcache, kv));
     TRY(dalloc(s, &s->d_vcache, kv));
     TRY(dalloc(s, &s->d_hidden, s->hidden));
     TRY(dalloc(s, &s->d_normed, s->hidden));
     TRY(dalloc(s, &s->d_final, s->hidden));
     TRY(dalloc(s, &s->d_proj, s->hidden));
-    TRY(dalloc(s, &s->d_q, s->q_width));
-    TRY(dalloc(s, &s->d_qrot, s->q_width));
+    TRY(dalloc(s, &s->d_q, s->q_local));
+    TRY(dalloc(s, &s->d_qrot, s->q_local));
     TRY(dalloc(s, &s->d_ctx, s->q_width));
-    TRY(dalloc(s, &s->d_k, s->kv_width));
-    TRY(dalloc(s, &s->d_v, s->kv_width));
-    TRY(dalloc(s, &s->d_gate, s->ffn));
-    TRY(dalloc(s, &s->d_up, s->ffn));
+    if (s->qmax) TRY(dalloc(s, &s->d_ctx_pad, (size_t)s->world * s->qmax * s->head_dim));
+    TRY(dalloc(s, &s->d_k, s->kv_local));
+    TRY(dalloc(s, &s->d_v, s->kv_local));
+    TRY(dalloc(s, &s->d_gate, s->f1 - s->f0));
+    TRY(dalloc(s, &s->d_up, s->f1 - s->f0));
     TRY(dalloc(s, &s->d_act, s->ffn));
     TRY(dalloc(s, &s->d_logits, s->vocab));
     TRY(dalloc(s, &s->d_ints, 8));
@@ -244,8 +287,10 @@ int session_alloc_state(satori_session *s)
     s->d_tokens = s->d_ints + 2;
     s->d_argmax = s->d_ints + 3;
     s->d_nonfinite = s->d_ints + 4;
+    // Enough partial records for any launch shape the step uses (a single KV head has the most splits).
     TRY(dalloc(s, &s->d_attn_scratch,
-               attn_scratch_floats(s->q_heads, s->kv_heads, s->head_dim, s->context, s->ctx->sm_count)));
+               std::max(attn_scratch_floats(s->q_heads, s->kv_heads, s->head_dim, s->context, s->ctx->sm_count),
+                        attn_scratch_floats(s->q_heads, 1, s->head_dim, s->context, s->ctx->sm_count))));
     TRYCUDA(cudaHostAlloc(&s->h_ints, 8 * sizeof(int), cudaHostAllocDefault), "pinned ints");
     TRYCUDA(cudaHostAlloc(&s->h_logits, (size_t)s->vocab * 4, cudaHostAllocDefault), "pinned logits");
     return SATORI_OK;
@@ -263,10 +308,8 @@ static int check_desc(const satori_model_desc *d, int context)
     return SATORI_OK;
 }
 
-extern "C" int satori_session_create(satori_ctx *ctx, const satori_model_desc *d, int context, satori_session **out)
+satori_session *session_new(satori_ctx *ctx, const satori_model_desc *d, int context)
 {
-    if (!ctx || !out) return set_error(SATORI_ERR_ARGUMENT, "null argument");
-    TRY(check_desc(d, context));
     satori_session *s = new satori_session();
     s->ctx = ctx;
     s->layers = d->layers;
@@ -282,7 +325,15 @@ extern "C" int satori_session_create(satori_ctx *ctx, const satori_model_desc *d
     s->q_width = d->q_heads * d->head_dim;
     s->kv_width = d->kv_heads * d->head_dim;
     s->use_pdl = 1;
-    int rc = session_upload(s, d);
+    return s;
+}
+
+// Uploads this rank's weights, allocates the state and captures the decode step.  On failure the
+// session is destroyed and the error of the failing call is kept.
+int session_build(satori_session *s, const satori_model_desc *d, satori_session **out)
+{
+    int rc = session_plan_shards(s);
+    if (!rc) rc = session_upload(s, d);
     if (!rc) rc = session_alloc_state(s);
     if (!rc) rc = build_graph(s);
     if (rc) {
@@ -294,6 +345,15 @@ extern "C" int satori_session_create(satori_ctx *ctx, const satori_model_desc *d
     }
     *out = s;
     return SATORI_OK;
+}
+
+int session_check_desc(const satori_model_desc *d, int context) { return check_desc(d, context); }
+
+extern "C" int satori_session_create(satori_ctx *ctx, const satori_model_desc *d, int context, satori_session **out)
+{
+    if (!ctx || !out) return set_error(SATORI_ERR_ARGUMENT, "null argument");
+    TRY(check_desc(d, context));
+    return session_build(session_new(ctx, d, context), d, out);
 }
 
 // Runs `count` steps fed from host tokens `feed` (one step per token).

@@ -50,8 +50,30 @@ struct satori_session {
     cudaGraphExec_t graph_exec = nullptr;
     std::vector<void *> allocations;
 
+    // This rank's share of every dimension (a single-GPU session is world 1, rank 0, full ranges).
+    // Rows stay whole on one rank, so every projection keeps the reference's per-row FP32 order.
+    int world = 1, rank = 0;
+    int qa = 0, qb = 0;              // query heads computed here
+    int ka = 0, kb = 0;              // KV heads computed and cached here (those of qa .. qb-1)
+    int h0 = 0, h1 = 0;              // rows of attn_output / ffn_down (hidden)
+    int f0 = 0, f1 = 0;              // rows of ffn_gate / ffn_up
+    int v0 = 0, v1 = 0;              // rows of the logits matrix
+    int q_local = 0, kv_local = 0;   // floats of this rank's q and k (or v) vectors
+    int qmax = 0;                    // query heads per rank in the padded context exchange (0: none)
+    float *d_ctx_pad = nullptr;      // [world][qmax * head_dim] when query heads do not split evenly
+
     ShardState *shard = nullptr;
 };
 
+satori_session *session_new(satori_ctx *ctx, const satori_model_desc *d, int context);
+int session_check_desc(const satori_model_desc *d, int context);
+int session_build(satori_session *s, const satori_model_desc *d, satori_session **out);
 int session_alloc_state(satori_session *s);
 void session_destroy_sharding(satori_session *s);
+// Fills the rank's ranges (world 1: everything).  Returns a satori_status.
+int session_plan_shards(satori_session *s);
+// In-place all-gather of `count` floats per rank: rank r's slice is buf + r * count.  No-op for world 1.
+int session_allgather(satori_session *s, float *buf, size_t count, cudaStream_t st);
+// Copies every rank's query-head block out of the padded exchange buffer into d_ctx.
+cudaError_t launch_ctx_compact(const float *pad, float *ctx, int world, int q_heads, int head_dim, int qmax,
+                               cudaStream_t st);

@@ -14,7 +14,7 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from . import _lib
-from ._lib import ArgumentError, DisposedError, check
+from ._lib import ArgumentError, DisposedError, NotSupportedError, check
 from .core import Context, default_context
 
 _vp = C.c_void_p
@@ -148,6 +148,37 @@ def build_desc(spec: ModelSpec, tensors: dict):
     d.tensors = C.cast(arr, C.POINTER(_lib.Tensor))
     keep.append(arr)
     return d, keep
+
+
+def nccl_unique_id() -> bytes:
+    """The 128-byte NCCL id rank 0 creates and sends to every rank of a sharded session."""
+    buf = C.create_string_buffer(128)
+    check(_lib.lib().satori_nccl_unique_id(buf), "nccl_unique_id")
+    return buf.raw
+
+
+def broadcast_nccl_id(group=None) -> bytes:
+    """Rank 0's NCCL id delivered to every rank of a torch.distributed group (the group only carries
+    the 128 bytes; the session's exchanges run on its own NCCL communicator)."""
+    import torch.distributed as dist
+    obj = [nccl_unique_id() if dist.get_rank(group) == 0 else None]
+    dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+    return obj[0]
+
+
+def shard_ranges(spec: ModelSpec, rank: int, world: int) -> dict:
+    """Rows and heads rank `rank` of `world` computes in a sharded session (mirrors session_plan_shards):
+    contiguous row blocks of every projection, query heads [q0, q1) and the KV heads they read."""
+    if world == 1:
+        return {"hidden": (0, spec.hidden), "ffn": (0, spec.ffn), "vocab": (0, spec.vocab),
+                "q_heads": (0, spec.q_heads), "kv_heads": (0, spec.kv_heads)}
+    if spec.hidden % world or spec.ffn % world or spec.vocab % world or spec.q_heads < world:
+        raise NotSupportedError(_lib.ERR_NOT_SUPPORTED, "shape does not shard over %d ranks" % world)
+    group = spec.q_heads // spec.kv_heads
+    qa, qb = rank * spec.q_heads // world, (rank + 1) * spec.q_heads // world
+    step = lambda n: (rank * (n // world), (rank + 1) * (n // world))
+    return {"hidden": step(spec.hidden), "ffn": step(spec.ffn), "vocab": step(spec.vocab), "q_heads": (qa, qb),
+            "kv_heads": (qa // group, (qb - 1) // group + 1)}
 
 
 class CudaDenseSession:

@@ -1,0 +1,98 @@
+"""Sharded decode session (one process per GPU, NCCL all-gathers) vs the oracle's DenseSession.
+
+Projections are sharded by rows, so every logit is produced by the same per-row FP32 chain as on
+one GPU; attention is sharded by query heads.  Every rank must hold the same full logits (bitwise:
+they are all-gathered), within the single-GPU tolerance of the oracle, with identical greedy tokens.
+The shapes cover an even head split, a split that cuts a GQA group (two ranks compute one KV head),
+and an uneven query-head split (padded context exchange).
+"""
+import multiprocessing as mp
+import os
+
+import numpy as np
+import pytest
+
+from model_util import synthetic_tensors
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_REL, LOGIT_ABS = 1e-4, 1e-5
+CHILD_TIMEOUT_S = 300
+
+
+def _gpu_count() -> int:
+    import torch
+    return torch.cuda.device_count()
+
+
+@pytest.fixture(scope="module")
+def sat():
+    from satori_b200 import build
+    build.build()
+    import satori_b200
+    return satori_b200
+
+
+def _run_world(sat, world, spec_kwargs, seed, context, tokens, gen_first, gen_count, tmp_path):
+    import shard_worker
+    nccl_id = sat.nccl_unique_id()
+    mpc = mp.get_context("spawn")
+    outs = [str(tmp_path / ("rank%d.npz" % r)) for r in range(world)]
+    old = os.environ.get("NCCL_NVLS_ENABLE")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        procs = [mpc.Process(target=shard_worker.run_rank,
+                             args=(r, world, nccl_id, spec_kwargs, seed, context, tokens, gen_first, gen_count,
+                                   outs[r]))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(CHILD_TIMEOUT_S)
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+                p.join()
+    finally:
+        if old is None:
+            os.environ.pop("NCCL_NVLS_ENABLE", None)
+        else:
+            os.environ["NCCL_NVLS_ENABLE"] = old
+    assert [p.exitcode for p in procs] == [0] * world
+    return [np.load(o) for o in outs]
+
+
+CASES = [
+    # (world, tiny() overrides): even split; a split inside a GQA group; an uneven query-head split
+    (2, dict(layers=2, hidden=256, ffn=512, q_heads=4, kv_heads=2, head_dim=64, vocab=1000)),
+    (2, dict(layers=2, hidden=384, ffn=768, q_heads=6, kv_heads=3, head_dim=64, vocab=1000, proj_format=1)),
+    (2, dict(layers=3, hidden=192, ffn=384, q_heads=3, kv_heads=1, head_dim=64, vocab=1002, has_bias=False)),
+    (4, dict(layers=2, hidden=384, ffn=768, q_heads=6, kv_heads=2, head_dim=64, vocab=1000)),
+]
+
+
+@pytest.mark.parametrize("world,kw", CASES)
+def test_sharded_session_matches_oracle(sat, oracle_lib, tmp_path, world, kw):
+    if _gpu_count() < world:
+        pytest.skip("needs %d GPUs" % world)
+    from oracle.oracle import OracleSession
+    spec = sat.tiny(**kw)
+    tokens = [int(t) for t in np.random.default_rng(world + kw["q_heads"]).integers(0, spec.vocab, 20)]
+    res = _run_world(sat, world, kw, seed=17, context=48, tokens=tokens, gen_first=tokens[0], gen_count=12,
+                     tmp_path=tmp_path)
+    for r in range(1, world):
+        assert np.array_equal(res[r]["logits"].view(np.uint32), res[0]["logits"].view(np.uint32))
+        assert np.array_equal(res[r]["gen"], res[0]["gen"])
+    ref = OracleSession(spec, synthetic_tensors(spec, 17), 48)
+    for i, t in enumerate(tokens):
+        lr, ar = ref.append(t, threads=8)
+        lg = res[0]["logits"][i]
+        err = np.abs(lg.astype(np.float64) - lr)
+        assert np.all(err <= LOGIT_REL * np.abs(lr) + LOGIT_ABS), (i, float(err.max()))
+        assert int(res[0]["greedy"][i]) == ar, i
+    ref = OracleSession(spec, synthetic_tensors(spec, 17), 48)
+    t, expect = tokens[0], []
+    for _ in range(12):
+        _, t = ref.append(t, threads=8)
+        expect.append(t)
+    assert list(res[0]["gen"]) == expect
