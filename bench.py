@@ -452,7 +452,8 @@ def bench_decode(args, rank, world, local, spec):
             "dtype": "quantized weights, f32 activations", "data": "synthetic seeded weights, random prompt",
             "config": {"workload": spec.name, "prompt": args.prompt, "decode": args.decode,
                        "parallelism": "single GPU" if world == 1 else
-                       f"tp{world}: row-sharded projections, query-head-sharded attention, NCCL all-gathers"},
+                       f"tp{world}: row-sharded projections, query-head-sharded attention, all-gathers",
+                       "exchange": None if world == 1 else os.environ.get("SATORI_EXCHANGE", "p2p")},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
                          "algorithmic_bytes_per_launch": wbytes + kv_avg},

@@ -23,17 +23,6 @@
 
 using namespace satori;
 
-#define TRY(x)               \
-    do {                     \
-        int rc_ = (x);       \
-        if (rc_) return rc_; \
-    } while (0)
-#define TRYCUDA(x, what)                                   \
-    do {                                                   \
-        cudaError_t e_ = (x);                              \
-        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
-    } while (0)
-
 namespace {
 
 const satori_tensor *find_tensor(const satori_model_desc *d, const std::string &name)
@@ -171,17 +160,15 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
             a.use_pdl = pdl;
             TRYCUDA(launch_attention(a, s->ctx->sm_count, st), "attention");
         }
-        if (s->world > 1) {
-            if (s->qmax) {
-                TRY(session_allgather(s, s->d_ctx_pad, (size_t)s->qmax * hd, st));
-                TRYCUDA(launch_ctx_compact(s->d_ctx_pad, s->d_ctx, s->world, s->q_heads, hd, s->qmax, st), "ctx");
-            } else {
-                TRY(session_allgather(s, s->d_ctx, (size_t)s->q_local, st));
-            }
+        if (s->qmax) {
+            TRY(session_allgather(s, s->d_ctx_pad, (size_t)s->qmax * hd, st));
+            TRYCUDA(launch_ctx_compact(s->d_ctx_pad, s->d_ctx, s->world, s->q_heads, hd, s->qmax, st), "ctx");
+        } else {
+            TRY(session_exchange(s, s->d_ctx, (size_t)s->qa * hd, (size_t)s->q_local, st));
         }
         TRY(run_gemv(s->ctx, L.o.payload, s->h1 - s->h0, qw, L.o.format, SATORI_ORDER_BATCH, s->d_ctx,
                      s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl));
-        TRY(session_allgather(s, s->d_hidden, (size_t)(s->h1 - s->h0), st));
+        TRY(session_exchange(s, s->d_hidden, (size_t)s->h0, (size_t)(s->h1 - s->h0), st));
         TRYCUDA(launch_rmsnorm(s->d_hidden, L.ffn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
         const int nf = s->f1 - s->f0;
         TRY(run_gemv(s->ctx, L.gate.payload, nf, H, L.gate.format, SATORI_ORDER_BATCH, s->d_normed, s->d_gate, 1,
@@ -189,15 +176,15 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
         TRY(run_gemv(s->ctx, L.up.payload, nf, H, L.up.format, SATORI_ORDER_BATCH, s->d_normed, s->d_up, 1, kEpiNone,
                      nullptr, nullptr, st, pdl));
         TRYCUDA(launch_swiglu(s->d_gate, s->d_up, nf, s->d_act + s->f0, st, pdl), "swiglu");
-        TRY(session_allgather(s, s->d_act, (size_t)nf, st));
+        TRY(session_exchange(s, s->d_act, (size_t)s->f0, (size_t)nf, st));
         TRY(run_gemv(s->ctx, L.down.payload, s->h1 - s->h0, s->ffn, L.down.format, SATORI_ORDER_BATCH, s->d_act,
                      s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl));
-        TRY(session_allgather(s, s->d_hidden, (size_t)(s->h1 - s->h0), st));
+        TRY(session_exchange(s, s->d_hidden, (size_t)s->h0, (size_t)(s->h1 - s->h0), st));
     }
     TRYCUDA(launch_rmsnorm(s->d_hidden, s->output_norm, H, s->eps, s->d_final, st, pdl), "final norm");
     TRY(run_gemv(s->ctx, s->output.payload, s->v1 - s->v0, H, s->output.format, SATORI_ORDER_BATCH, s->d_final,
                  s->d_logits + s->v0, 1, kEpiNone, nullptr, nullptr, st, pdl));
-    TRY(session_allgather(s, s->d_logits, (size_t)(s->v1 - s->v0), st));
+    TRY(session_exchange(s, s->d_logits, (size_t)s->v0, (size_t)(s->v1 - s->v0), st));
     TRYCUDA(launch_argmax_advance(s->d_logits, s->vocab, s->d_argmax, s->d_nonfinite, s->d_pos, s->d_token, st, pdl),
             "argmax");
     return SATORI_OK;
@@ -267,20 +254,25 @@ int session_alloc_state(satori_session *s)
     const size_t kv = (size_t)s->layers * s->context * s->kv_local;
     TRY(dalloc(s, &s->d_kcache, kv));
     TRY(dalloc(s, &s->d_vcache, kv));
-    TRY(dalloc(s, &s->d_hidden, s->hidden));
+    // The vectors a sharded rank gathers live in the IPC-mapped exchange arena under the P2P backend.
+    if (session_p2p(s)) {
+        TRY(session_exchange_alloc(s));
+    } else {
+        TRY(dalloc(s, &s->d_hidden, s->hidden));
+        TRY(dalloc(s, &s->d_ctx, s->q_width));
+        TRY(dalloc(s, &s->d_act, s->ffn));
+        TRY(dalloc(s, &s->d_logits, s->vocab));
+    }
     TRY(dalloc(s, &s->d_normed, s->hidden));
     TRY(dalloc(s, &s->d_final, s->hidden));
     TRY(dalloc(s, &s->d_proj, s->hidden));
     TRY(dalloc(s, &s->d_q, s->q_local));
     TRY(dalloc(s, &s->d_qrot, s->q_local));
-    TRY(dalloc(s, &s->d_ctx, s->q_width));
     if (s->qmax) TRY(dalloc(s, &s->d_ctx_pad, (size_t)s->world * s->qmax * s->head_dim));
     TRY(dalloc(s, &s->d_k, s->kv_local));
     TRY(dalloc(s, &s->d_v, s->kv_local));
     TRY(dalloc(s, &s->d_gate, s->f1 - s->f0));
     TRY(dalloc(s, &s->d_up, s->f1 - s->f0));
-    TRY(dalloc(s, &s->d_act, s->ffn));
-    TRY(dalloc(s, &s->d_logits, s->vocab));
     TRY(dalloc(s, &s->d_ints, 8));
     s->d_token = s->d_ints + 0;
     s->d_pos = s->d_ints + 1;
@@ -357,9 +349,26 @@ extern "C" int satori_session_create(satori_ctx *ctx, const satori_model_desc *d
 }
 
 // Runs `count` steps fed from host tokens `feed` (one step per token).
+static int peer_lost(satori_session *s)
+{
+    return set_error(SATORI_ERR_TIMEOUT, "a peer rank stopped answering; destroy the sharded session");
+}
+
+// A bounded wait that expired in a sharded step means a peer is gone: the ranks are out of step.
+static int step_status(satori_session *s)
+{
+    const int rc = check_dev_error(s->ctx);
+    if (rc == SATORI_ERR_TIMEOUT && s->world > 1) {
+        s->failed = true;
+        return peer_lost(s);
+    }
+    return rc;
+}
+
 static int run_steps(satori_session *s, const int *feed, int count, float *logits, int *argmax)
 {
     if (!s) return set_error(SATORI_ERR_DISPOSED, "session is disposed");
+    if (s->failed) return peer_lost(s);
     if (count <= 0) return set_error(SATORI_ERR_ARGUMENT, "count must be positive");
     for (int i = 0; i < count; ++i)
         if (feed[i] < 0 || feed[i] >= s->vocab)
@@ -379,7 +388,7 @@ static int run_steps(satori_session *s, const int *feed, int count, float *logit
     TRYCUDA(cudaMemcpyAsync(s->h_ints, s->d_ints, 7 * sizeof(int), cudaMemcpyDeviceToHost, st), "state");
     if (logits)
         TRYCUDA(cudaMemcpyAsync(s->h_logits, s->d_logits, (size_t)s->vocab * 4, cudaMemcpyDeviceToHost, st), "logits");
-    int rc = check_dev_error(ctx);
+    int rc = step_status(s);
     s->position += count;
     if (rc) return rc;
     if (s->h_ints[4]) {
@@ -405,6 +414,7 @@ extern "C" int satori_session_append_tokens(satori_session *s, const int *tokens
 extern "C" int satori_session_generate(satori_session *s, int first, int count, int *tokens_out)
 {
     if (!s) return set_error(SATORI_ERR_DISPOSED, "session is disposed");
+    if (s->failed) return peer_lost(s);
     if (!tokens_out) return set_error(SATORI_ERR_ARGUMENT, "tokens_out is null");
     if (first < 0 || first >= s->vocab) return set_error(SATORI_ERR_ARGUMENT, "Token %d is outside the vocabulary.", first);
     if (count <= 0) return set_error(SATORI_ERR_ARGUMENT, "count must be positive");
@@ -427,7 +437,7 @@ extern "C" int satori_session_generate(satori_session *s, int first, int count, 
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     cudaFree(d_out);
     if (e != cudaSuccess) return cuda_fail(e, "generate");
-    int rc = check_dev_error(s->ctx);
+    int rc = step_status(s);
     s->position += count;
     if (rc) return rc;
     if (s->h_ints[4]) {

@@ -8,6 +8,17 @@
 
 #include "capi_internal.h"
 
+#define TRY(x)               \
+    do {                     \
+        int rc_ = (x);       \
+        if (rc_) return rc_; \
+    } while (0)
+#define TRYCUDA(x, what)                                   \
+    do {                                                   \
+        cudaError_t e_ = (x);                              \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
 struct DevMatrix {
     const uint8_t *payload = nullptr;
     int rows = 0, cols = 0, format = 0;
@@ -63,6 +74,7 @@ struct satori_session {
     float *d_ctx_pad = nullptr;      // [world][qmax * head_dim] when query heads do not split evenly
 
     ShardState *shard = nullptr;
+    bool failed = false;             // a peer stopped answering: every later step is refused
 };
 
 satori_session *session_new(satori_ctx *ctx, const satori_model_desc *d, int context);
@@ -72,8 +84,14 @@ int session_alloc_state(satori_session *s);
 void session_destroy_sharding(satori_session *s);
 // Fills the rank's ranges (world 1: everything).  Returns a satori_status.
 int session_plan_shards(satori_session *s);
-// In-place all-gather of `count` floats per rank: rank r's slice is buf + r * count.  No-op for world 1.
+// In-place NCCL all-gather of `count` floats per rank: rank r's slice is buf + r * count.  No-op for world 1.
 int session_allgather(satori_session *s, float *buf, size_t count, cudaStream_t st);
+// True when the gathered vectors are exchanged by peer stores (the default sharded backend).
+bool session_p2p(const satori_session *s);
+// Places d_hidden, d_ctx, d_act and d_logits in this rank's exchange arena and maps every peer's.
+int session_exchange_alloc(satori_session *s);
+// Gathers buf[off, off + count) from every rank (each rank its own slice) into every rank's buf.
+int session_exchange(satori_session *s, float *buf, size_t off, size_t count, cudaStream_t st);
 // Copies every rank's query-head block out of the padded exchange buffer into d_ctx.
 cudaError_t launch_ctx_compact(const float *pad, float *ctx, int world, int q_heads, int head_dim, int qmax,
                                cudaStream_t st);

@@ -32,3 +32,36 @@ def run_rank(rank: int, world: int, nccl_id: bytes, spec_kwargs: dict, seed: int
     with open(tmp, "wb") as f:
         np.savez(f, logits=np.stack(logits), greedy=np.array(greedy, np.int32), gen=gen)
     os.replace(tmp, out_path)
+
+
+def run_silent_peer(rank: int, world: int, nccl_id: bytes, spec_kwargs: dict, seed: int, done, out_path: str) -> None:
+    """Rank 0 steps alone while the other ranks stay idle between steps: rank 0's exchange wait must
+    expire with a timeout status (and latch it), and no rank may have a kernel left in flight."""
+    import time
+
+    import satori_b200 as sat
+    from model_util import synthetic_tensors
+
+    spec = sat.tiny(**spec_kwargs)
+    s = sat.CudaDenseSession(spec, synthetic_tensors(spec, seed), 16, ctx=sat.Context(rank), rank=rank, world=world,
+                             nccl_id=nccl_id)
+    result = {}
+    if rank == 0:
+        t0 = time.perf_counter()
+        try:
+            s.append(1)
+            result["first"] = "ok"
+        except sat.SatoriError as e:
+            result["first"] = e.status
+        result["first_s"] = time.perf_counter() - t0
+        try:
+            s.append(2)
+            result["second"] = "ok"
+        except sat.SatoriError as e:
+            result["second"] = e.status
+        done.set()
+    else:
+        done.wait(120)
+    s.dispose()
+    with open(out_path, "w") as f:
+        f.write(repr(result))

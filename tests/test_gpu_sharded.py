@@ -33,32 +33,39 @@ def sat():
     return satori_b200
 
 
-def _run_world(sat, world, spec_kwargs, seed, context, tokens, gen_first, gen_count, tmp_path):
-    import shard_worker
-    nccl_id = sat.nccl_unique_id()
+def _spawn(target, argsets, env):
+    """Starts one spawned child per rank with `env` added to the environment; returns their exit codes."""
     mpc = mp.get_context("spawn")
-    outs = [str(tmp_path / ("rank%d.npz" % r)) for r in range(world)]
-    old = os.environ.get("NCCL_NVLS_ENABLE")
-    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    saved = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
     try:
-        procs = [mpc.Process(target=shard_worker.run_rank,
-                             args=(r, world, nccl_id, spec_kwargs, seed, context, tokens, gen_first, gen_count,
-                                   outs[r]))
-                 for r in range(world)]
+        procs = [mpc.Process(target=target, args=a) for a in argsets]
         for p in procs:
             p.start()
-        for p in procs:
-            p.join(CHILD_TIMEOUT_S)
-        for p in procs:
-            if p.is_alive():
-                p.kill()
-                p.join()
     finally:
-        if old is None:
-            os.environ.pop("NCCL_NVLS_ENABLE", None)
-        else:
-            os.environ["NCCL_NVLS_ENABLE"] = old
-    assert [p.exitcode for p in procs] == [0] * world
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    for p in procs:
+        p.join(CHILD_TIMEOUT_S)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    return [p.exitcode for p in procs]
+
+
+def _run_world(sat, world, spec_kwargs, seed, context, tokens, gen_first, gen_count, tmp_path, backend):
+    import shard_worker
+    nccl_id = sat.nccl_unique_id()
+    outs = [str(tmp_path / ("rank%d.npz" % r)) for r in range(world)]
+    codes = _spawn(shard_worker.run_rank,
+                   [(r, world, nccl_id, spec_kwargs, seed, context, tokens, gen_first, gen_count, outs[r])
+                    for r in range(world)],
+                   {"NCCL_NVLS_ENABLE": "0", "SATORI_EXCHANGE": backend})
+    assert codes == [0] * world
     return [np.load(o) for o in outs]
 
 
@@ -71,15 +78,16 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("backend", ["p2p", "nccl"])
 @pytest.mark.parametrize("world,kw", CASES)
-def test_sharded_session_matches_oracle(sat, oracle_lib, tmp_path, world, kw):
+def test_sharded_session_matches_oracle(sat, oracle_lib, tmp_path, world, kw, backend):
     if _gpu_count() < world:
         pytest.skip("needs %d GPUs" % world)
     from oracle.oracle import OracleSession
     spec = sat.tiny(**kw)
     tokens = [int(t) for t in np.random.default_rng(world + kw["q_heads"]).integers(0, spec.vocab, 20)]
     res = _run_world(sat, world, kw, seed=17, context=48, tokens=tokens, gen_first=tokens[0], gen_count=12,
-                     tmp_path=tmp_path)
+                     tmp_path=tmp_path, backend=backend)
     for r in range(1, world):
         assert np.array_equal(res[r]["logits"].view(np.uint32), res[0]["logits"].view(np.uint32))
         assert np.array_equal(res[r]["gen"], res[0]["gen"])
@@ -96,3 +104,23 @@ def test_sharded_session_matches_oracle(sat, oracle_lib, tmp_path, world, kw):
         _, t = ref.append(t, threads=8)
         expect.append(t)
     assert list(res[0]["gen"]) == expect
+
+
+def test_silent_peer_times_out_and_latches(sat, tmp_path):
+    """Failure detection without a GPU fault: rank 1 never steps, so rank 0's first exchange finds no
+    signal; its bounded wait expires (0.5 s here), the step reports a timeout, and the session refuses
+    later steps.  Rank 1 has no kernel in flight and both ranks dispose normally."""
+    if _gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import ast
+
+    import shard_worker
+    nccl_id = sat.nccl_unique_id()
+    done = mp.get_context("spawn").Event()
+    outs = [str(tmp_path / ("silent%d.txt" % r)) for r in range(2)]
+    codes = _spawn(shard_worker.run_silent_peer, [(r, 2, nccl_id, {}, 5, done, outs[r]) for r in range(2)],
+                   {"NCCL_NVLS_ENABLE": "0", "SATORI_EXCHANGE": "p2p", "SATORI_PEER_TIMEOUT_MS": "500"})
+    assert codes == [0, 0]
+    r0 = ast.literal_eval(open(outs[0]).read())
+    assert r0["first"] == sat._lib.ERR_TIMEOUT and r0["second"] == sat._lib.ERR_TIMEOUT
+    assert 0.4 < r0["first_s"] < 30
