@@ -577,7 +577,7 @@ __global__ void rope_append_kernel(RopeAppendArgs a)
     float *kslot = a.k_cache + (long long)pos * kvw;
     float *vslot = a.v_cache + (long long)pos * kvw;
     // TransformerOps.RopeHalf (TransformerOps.cs:99-118): FP64 angle and rotation, FP32 result.
-    for (int i = threadIdx.x; i < qw + 2 * kvw; i += blockDim.x) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < qw + 2 * kvw; i += gridDim.x * blockDim.x) {
         if (i < qw + kvw) {
             const bool isq = i < qw;
             const int e = isq ? i : i - qw;
@@ -587,9 +587,14 @@ __global__ void rope_append_kernel(RopeAppendArgs a)
             float r;
             if (d < a.rotary) {
                 const int k = d < half ? d : d - half;
-                const double angle = __ddiv_rn((double)pos, pow(a.base, __ddiv_rn(2.0 * k, (double)a.rotary)));
                 double sn, cs;
-                sincos(angle, &sn, &cs);
+                if (a.table) {
+                    cs = a.table[2 * k];
+                    sn = a.table[2 * k + 1];
+                } else {
+                    const double angle = __ddiv_rn((double)pos, pow(a.base, __ddiv_rn(2.0 * k, (double)a.rotary)));
+                    sincos(angle, &sn, &cs);
+                }
                 const double x = src[base_i + k], y = src[base_i + k + half];
                 r = d < half ? (float)__dsub_rn(__dmul_rn(x, cs), __dmul_rn(y, sn))
                              : (float)__dadd_rn(__dmul_rn(x, sn), __dmul_rn(y, cs));
@@ -754,9 +759,10 @@ cudaError_t launch_attention(const AttnArgs &a, int sm_count, cudaStream_t strea
 
 cudaError_t launch_rope_append(const RopeAppendArgs &a, cudaStream_t stream)
 {
+    const int n = (a.q_heads + 2 * a.kv_heads) * a.head_dim;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(1);
-    cfg.blockDim = dim3(512);
+    cfg.gridDim = dim3(a.table ? (n + 255) / 256 : 1);
+    cfg.blockDim = dim3(a.table ? 256 : 512);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -37,6 +37,7 @@ struct RopeAppendArgs {
     double base;
     int position;
     const int *position_dev;
+    const double *table;        // optional [rotary/2][cos, sin] for this position (launch_embed writes it)
     int use_pdl;
 };
 cudaError_t launch_rope_append(const RopeAppendArgs &a, cudaStream_t stream);

@@ -149,6 +149,8 @@ int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int 
                 continue;
             }
         }
+        if (epilogue == kEpiSwiGlu)
+            return set_error(SATORI_ERR_NOT_SUPPORTED, "the fused SwiGLU epilogue needs the decode rows kernel");
         GemvPlan plan = plan_gemv(rows, cols, format, np, ctx->sm_count, ctx->smem_optin);
         if (!plan.ok) return set_error(SATORI_ERR_ARGUMENT, "no MatVec plan fits shared memory for %dx%d", rows, cols);
         GemvArgs a = {};

@@ -43,6 +43,21 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t bits16)
     return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFFu)));
 }
 
+// TransformerOps.SwiGlu (TransformerOps.cs:41-51) for one element: FP64 sigmoid of the gate, every
+// multiply and add rounded separately, FP32 result.
+__device__ __forceinline__ float swiglu_value(float gate, float up)
+{
+    const double x = gate;
+    double sig;
+    if (x >= 0) {
+        sig = __ddiv_rn(1.0, __dadd_rn(1.0, exp(-x)));
+    } else {
+        const double e = exp(x);
+        sig = __ddiv_rn(e, __dadd_rn(1.0, e));
+    }
+    return (float)__dmul_rn(__dmul_rn(x, sig), (double)up);
+}
+
 // --------------------------------------------------------------------------- shared memory
 __device__ __forceinline__ uint32_t smem_u32(const void *p)
 {

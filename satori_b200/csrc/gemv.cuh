@@ -11,7 +11,9 @@ namespace satori {
 //   y = acc + bias                (kEpiBias: TransformerOps.Add(query, bias, query), DenseForward.cs:124-129)
 //   y = residual + acc, residual := y  (kEpiResidual: TransformerOps.Add(residual, projected, residual),
 //                                      DenseForward.cs:148,160)
-enum Epilogue : int { kEpiNone = 0, kEpiBias = 1, kEpiResidual = 2 };
+//   y[r/2] = SwiGlu(acc[r], acc[r+1]) for even r  (kEpiSwiGlu: rows interleave ffn_gate and ffn_up row by
+//                                      row; TransformerOps.SwiGlu, DenseForward.cs:151-153; gemv_rows only)
+enum Epilogue : int { kEpiNone = 0, kEpiBias = 1, kEpiResidual = 2, kEpiSwiGlu = 3 };
 
 struct GemvArgs {
     const uint8_t *payload;  // device, 256-byte aligned, readable 16 bytes past the end
@@ -37,13 +39,16 @@ struct GemvPlan {
 GemvPlan plan_gemv(int rows, int cols, int format, int positions, int sm_count, size_t smem_limit);
 
 // Decode-order MatVec of one position for Q8_0 / Q4_0 with cols % 256 == 0: gemv_rows.cu (up to
-// 8192 columns, kind 1) and gemv_decode.cu (column chunks, any width, kind 2).  A plan function returns
+// 24576 columns, kind 1) and gemv_decode.cu (column chunks, any width, kind 2).  A plan function returns
 // ok = 0 for any argument set its kernel does not take.
 struct DecodePlan {
     int ok, kind, grid, rc, stages, nchunks, rs;
+    int cw, nb, fold;     // gemv_rows: compute warps, block columns per lane, rows per fold batch
     size_t smem;
 };
 DecodePlan plan_gemv_rows(const GemvArgs &a, int sm_count, size_t smem_limit);
+// True when the decode-order rows kernel takes this shape (and so the fused SwiGLU epilogue).
+bool gemv_rows_takes(int rows, int cols, int format, int sm_count, size_t smem_limit);
 cudaError_t launch_gemv_rows(const GemvArgs &a, const DecodePlan &plan, cudaStream_t stream);
 DecodePlan plan_gemv_decode(const GemvArgs &a, int sm_count, size_t smem_limit);
 cudaError_t launch_gemv_decode(const GemvArgs &a, const DecodePlan &plan, cudaStream_t stream);

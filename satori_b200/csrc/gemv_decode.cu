@@ -377,7 +377,7 @@ DecodePlan plan_gemv_decode(const GemvArgs &a, int sm_count, size_t smem_limit)
 {
     DecodePlan p = {};
     if ((a.format != 0 && a.format != 1) || a.order != SATORI_ORDER_BATCH || a.positions != 1) return p;
-    if (a.cols <= 0 || a.cols % 256 != 0 || a.rows <= 0) return p;
+    if (a.cols <= 0 || a.cols % 256 != 0 || a.rows <= 0 || a.epilogue == kEpiSwiGlu) return p;
     if ((reinterpret_cast<uintptr_t>(a.payload) & 15) || (reinterpret_cast<uintptr_t>(a.x) & 15)) return p;
     if (!encode_fn()) return p;
     const int pitch = kChunkBlocks * blk_bytes(a.format);

@@ -1,5 +1,7 @@
 // ops.cu -- decode-step glue kernels.  FP64 where the reference computes in FP64, with every
 // multiply and add rounded separately (no contraction), as the reference does.
+#include <algorithm>
+
 #include "common.cuh"
 #include "ops.cuh"
 
@@ -67,24 +69,27 @@ __global__ void rmsnorm_heads_kernel(float *v, int n, const float *w, float eps,
 __global__ void swiglu_kernel(const float *gate, const float *up, int n, float *out, int pdl)
 {
     if (pdl) pdl_wait();
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const double x = gate[i];
-        double sig;
-        if (x >= 0) {
-            sig = __ddiv_rn(1.0, __dadd_rn(1.0, exp(-x)));
-        } else {
-            const double e = exp(x);
-            sig = __ddiv_rn(e, __dadd_rn(1.0, e));
-        }
-        out[i] = (float)__dmul_rn(__dmul_rn(x, sig), (double)up[i]);
-    }
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        out[i] = swiglu_value(gate[i], up[i]);
     if (pdl) pdl_launch_dependents();
 }
 
 __global__ void embed_kernel(const uint8_t *embd, int cols, const int *token_dev, const int *pos_dev, int *tokens_dev,
-                             float *hidden, int pdl)
+                             float *hidden, double *rope_table, double rope_base, int rotary, int pdl)
 {
     if (pdl) pdl_wait();
+    if (rope_table) {
+        // TransformerOps.RopeHalf (TransformerOps.cs:99-118): the FP64 angle of pair k and its sin/cos,
+        // the same for every head and layer of this step.
+        const int k = blockIdx.x * blockDim.x + threadIdx.x;
+        if (k < rotary / 2) {
+            const double angle = __ddiv_rn((double)*pos_dev, pow(rope_base, __ddiv_rn(2.0 * k, (double)rotary)));
+            double sn, cs;
+            sincos(angle, &sn, &cs);
+            rope_table[2 * k] = cs;
+            rope_table[2 * k + 1] = sn;
+        }
+    }
     const int token = *token_dev;
     const int bpr = cols / 32;
     const uint8_t *row = embd + (long long)token * bpr * 34;
@@ -105,35 +110,46 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx)
     return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
 }
 
-__global__ void __launch_bounds__(1024) argmax_kernel(const float *logits, int n, int *argmax, int *nonfinite, int *pos,
-                                                      int *token, int pdl)
+constexpr int kArgmaxThreads = 256;
+
+// Grid-wide: every CTA folds its share into one 64-bit key with atomicMax (the key orders by value,
+// then by the smaller index, so the result does not depend on the CTA order); the last CTA to finish
+// publishes the index and clears the scratch for the next launch.
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float *logits, int n, int *argmax,
+                                                                int *nonfinite, int *pos, int *token,
+                                                                unsigned *scratch, int pdl)
 {
-    __shared__ unsigned long long red[1024];
-    __shared__ int bad;
+    __shared__ unsigned long long red[kArgmaxThreads / 32];
+    unsigned long long *best_dev = reinterpret_cast<unsigned long long *>(scratch);
+    unsigned *ticket = scratch + 2;
     if (pdl) pdl_wait();
-    if (threadIdx.x == 0) bad = 0;
-    __syncthreads();
     unsigned long long best = 0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    bool bad = false;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const float v = logits[i];
-        if (!isfinite(v)) bad = 1;
+        bad |= !isfinite(v);
         const unsigned long long k = argmax_key(v, i);
         best = k > best ? k : best;
     }
-    red[threadIdx.x] = best;
+    if (__any_sync(0xFFFFFFFFu, bad) && (threadIdx.x & 31) == 0) *nonfinite = 1;
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_down_sync(0xFFFFFFFFu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
     __syncthreads();
-    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
-        if (threadIdx.x < s && red[threadIdx.x + s] > red[threadIdx.x]) red[threadIdx.x] = red[threadIdx.x + s];
-        __syncthreads();
-    }
-    if (threadIdx.x == 0) {
-        const int idx = (int)(0xFFFFFFFFu - (uint32_t)(red[0] & 0xFFFFFFFFull));
-        *argmax = idx;
-        *token = idx;
-        if (bad) *nonfinite = 1;
-        *pos = *pos + 1;
-    }
-    if (pdl) pdl_launch_dependents();
+    if (threadIdx.x != 0) return;
+    for (int w = 1; w < kArgmaxThreads / 32; ++w) best = red[w] > best ? red[w] : best;
+    atomicMax(best_dev, best);
+    __threadfence();
+    if (atomicAdd(ticket, 1u) != gridDim.x - 1) return;
+    __threadfence();
+    const unsigned long long k = atomicExch(best_dev, 0ull);
+    *ticket = 0;
+    const int idx = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+    *argmax = idx;
+    *token = idx;
+    *pos = *pos + 1;
 }
 
 }  // namespace
@@ -155,18 +171,19 @@ cudaError_t launch_swiglu(const float *gate, const float *up, int n, float *out,
 }
 
 cudaError_t launch_embed(const uint8_t *embd, int cols, const int *token_dev, const int *pos_dev, int *tokens_dev,
-                         float *hidden, cudaStream_t s, int pdl)
+                         float *hidden, double *rope_table, double rope_base, int rotary, cudaStream_t s, int pdl)
 {
-    const int blocks = (cols + 255) / 256;
+    const int blocks = (std::max(cols, rotary / 2) + 255) / 256;
     return launch_ex(embed_kernel, dim3(blocks), dim3(256), 0, s, pdl, embd, cols, token_dev, pos_dev, tokens_dev,
-                     hidden, pdl);
+                     hidden, rope_table, rope_base, rotary, pdl);
 }
 
 cudaError_t launch_argmax_advance(const float *logits, int n, int *argmax_dev, int *nonfinite_dev, int *pos_dev,
-                                  int *token_dev, cudaStream_t s, int pdl)
+                                  int *token_dev, unsigned *scratch, int sm_count, cudaStream_t s, int pdl)
 {
-    return launch_ex(argmax_kernel, dim3(1), dim3(1024), 0, s, pdl, logits, n, argmax_dev, nonfinite_dev, pos_dev,
-                     token_dev, pdl);
+    const int blocks = std::max(1, std::min(sm_count, (n + 4 * kArgmaxThreads - 1) / (4 * kArgmaxThreads)));
+    return launch_ex(argmax_kernel, dim3(blocks), dim3(kArgmaxThreads), 0, s, pdl, logits, n, argmax_dev,
+                     nonfinite_dev, pos_dev, token_dev, scratch, pdl);
 }
 
 }  // namespace satori

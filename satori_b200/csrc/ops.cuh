@@ -14,12 +14,15 @@ cudaError_t launch_rmsnorm_heads(float *v, int n, const float *w, float eps, int
 // TransformerOps.SwiGlu (:41-51): FP64 sigmoid.
 cudaError_t launch_swiglu(const float *gate, const float *up, int n, float *out, cudaStream_t s, int pdl);
 // DenseForward.Embed via GgufQuantizedMatrix.ReadRow (Q8_0 rows): token from *token_dev; also writes
-// *tokens_dev = *pos_dev + 1 (the attention prefix length of this step).
+// *tokens_dev = *pos_dev + 1 (the attention prefix length of this step).  With rope_table non-null it
+// also writes the step's RoPE factors (cos, sin of TransformerOps.RopeHalf's angle for pair k at
+// position *pos_dev, k < rotary/2) for every layer's rope_append to read.
 cudaError_t launch_embed(const uint8_t *embd, int cols, const int *token_dev, const int *pos_dev, int *tokens_dev,
-                         float *hidden, cudaStream_t s, int pdl);
+                         float *hidden, double *rope_table, double rope_base, int rotary, cudaStream_t s, int pdl);
 // GreedyTokenSelector.Select (src/Satori.Core/GreedyTokenSelector.cs:6-16): smallest index of the
 // maximum; a non-finite logit sets *nonfinite_dev.  Then advances *pos_dev and feeds *token_dev.
+// `scratch` = 4 zeroed words (8-byte aligned) the launch leaves zeroed again.
 cudaError_t launch_argmax_advance(const float *logits, int n, int *argmax_dev, int *nonfinite_dev, int *pos_dev,
-                                  int *token_dev, cudaStream_t s, int pdl);
+                                  int *token_dev, unsigned *scratch, int sm_count, cudaStream_t s, int pdl);
 
 }  // namespace satori

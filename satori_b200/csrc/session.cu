@@ -17,7 +17,12 @@
 
 #include <string.h>
 
+#include <stdlib.h>
+#include <string.h>
+
 #include <algorithm>
+#include <initializer_list>
+#include <utility>
 #include <string>
 #include <vector>
 
@@ -88,6 +93,67 @@ int fetch_vector(satori_session *s, const satori_model_desc *d, const std::strin
     return SATORI_OK;
 }
 
+void release(satori_session *s, void *p)
+{
+    if (!p) return;
+    cudaFree(p);
+    s->allocations.erase(std::find(s->allocations.begin(), s->allocations.end(), p));
+}
+
+// One payload holding the rows of `parts` stacked in order (interleave = false) or, for two parts of
+// equal height, row i of part 0 then row i of part 1 (interleave = true).  The parts are freed.
+int combine_rows(satori_session *s, std::initializer_list<DevMatrix *> parts, bool interleave, DevMatrix *out)
+{
+    const DevMatrix &p0 = **parts.begin();
+    const size_t rb = payload_bytes(1, p0.cols, p0.format);
+    int rows = 0;
+    for (const DevMatrix *p : parts) rows += p->rows;
+    uint8_t *d = nullptr;
+    const size_t bytes = (size_t)rows * rb;
+    TRYCUDA(cudaMalloc(&d, bytes + 256), "allocate fused payload");
+    s->allocations.push_back(d);
+    TRYCUDA(cudaMemset(d + bytes, 0, 256), "clear payload padding");
+    if (interleave) {
+        int k = 0;
+        for (const DevMatrix *p : parts)
+            TRYCUDA(cudaMemcpy2D(d + rb * k++, 2 * rb, p->payload, rb, rb, p->rows, cudaMemcpyDeviceToDevice),
+                    "interleave rows");
+    } else {
+        size_t off = 0;
+        for (const DevMatrix *p : parts) {
+            TRYCUDA(cudaMemcpy(d + off, p->payload, (size_t)p->rows * rb, cudaMemcpyDeviceToDevice), "stack rows");
+            off += (size_t)p->rows * rb;
+        }
+    }
+    for (DevMatrix *p : parts) {
+        release(s, const_cast<uint8_t *>(p->payload));
+        p->payload = nullptr;
+    }
+    out->payload = d;
+    out->rows = rows;
+    out->cols = p0.cols;
+    out->format = p0.format;
+    return SATORI_OK;
+}
+
+int stack_vectors(satori_session *s, std::initializer_list<std::pair<float **, int>> parts, float **out)
+{
+    int n = 0;
+    for (const auto &p : parts) n += p.second;
+    float *d = nullptr;
+    TRYCUDA(cudaMalloc(&d, (size_t)n * 4), "allocate fused bias");
+    s->allocations.push_back(d);
+    int off = 0;
+    for (const auto &p : parts) {
+        TRYCUDA(cudaMemcpy(d + off, *p.first, (size_t)p.second * 4, cudaMemcpyDeviceToDevice), "stack bias");
+        off += p.second;
+        release(s, *p.first);
+        *p.first = nullptr;
+    }
+    *out = d;
+    return SATORI_OK;
+}
+
 template <typename T>
 int dalloc(satori_session *s, T **p, size_t n)
 {
@@ -108,16 +174,23 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
     const int H = s->hidden, qw = s->q_width, hd = s->head_dim;
     const int group = s->q_heads / s->kv_heads;
     const int nq = s->qb - s->qa, nkv = s->kb - s->ka;
-    TRYCUDA(launch_embed(s->embd.payload, H, s->d_token, s->d_pos, s->d_tokens, s->d_hidden, st, pdl), "embed");
+    TRYCUDA(launch_embed(s->embd.payload, H, s->d_token, s->d_pos, s->d_tokens, s->d_hidden, s->d_rope, s->rope_base,
+                         hd, st, pdl),
+            "embed");
     for (int l = 0; l < s->layers; ++l) {
         const Layer &L = s->layer[l];
         TRYCUDA(launch_rmsnorm(s->d_hidden, L.attn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
-        TRY(run_gemv(s->ctx, L.q.payload, L.q.rows, H, L.q.format, SATORI_ORDER_BATCH, s->d_normed, s->d_q, 1,
-                     L.q_bias ? kEpiBias : kEpiNone, L.q_bias, nullptr, st, pdl));
-        TRY(run_gemv(s->ctx, L.k.payload, L.k.rows, H, L.k.format, SATORI_ORDER_BATCH, s->d_normed, s->d_k, 1,
-                     L.k_bias ? kEpiBias : kEpiNone, L.k_bias, nullptr, st, pdl));
-        TRY(run_gemv(s->ctx, L.v.payload, L.v.rows, H, L.v.format, SATORI_ORDER_BATCH, s->d_normed, s->d_v, 1,
-                     L.v_bias ? kEpiBias : kEpiNone, L.v_bias, nullptr, st, pdl));
+        if (L.qkv.payload) {
+            TRY(run_gemv(s->ctx, L.qkv.payload, L.qkv.rows, H, L.qkv.format, SATORI_ORDER_BATCH, s->d_normed, s->d_qkv,
+                         1, L.qkv_bias ? kEpiBias : kEpiNone, L.qkv_bias, nullptr, st, pdl));
+        } else {
+            TRY(run_gemv(s->ctx, L.q.payload, L.q.rows, H, L.q.format, SATORI_ORDER_BATCH, s->d_normed, s->d_q, 1,
+                         L.q_bias ? kEpiBias : kEpiNone, L.q_bias, nullptr, st, pdl));
+            TRY(run_gemv(s->ctx, L.k.payload, L.k.rows, H, L.k.format, SATORI_ORDER_BATCH, s->d_normed, s->d_k, 1,
+                         L.k_bias ? kEpiBias : kEpiNone, L.k_bias, nullptr, st, pdl));
+            TRY(run_gemv(s->ctx, L.v.payload, L.v.rows, H, L.v.format, SATORI_ORDER_BATCH, s->d_normed, s->d_v, 1,
+                         L.v_bias ? kEpiBias : kEpiNone, L.v_bias, nullptr, st, pdl));
+        }
         if (L.q_norm) {
             TRYCUDA(launch_rmsnorm_heads(s->d_q, s->q_local, L.q_norm, s->eps, hd, st, pdl), "q norm");
             TRYCUDA(launch_rmsnorm_heads(s->d_k, s->kv_local, L.k_norm, s->eps, hd, st, pdl), "k norm");
@@ -135,6 +208,7 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
         r.rotary = hd;
         r.base = s->rope_base;
         r.position_dev = s->d_pos;
+        r.table = s->d_rope;
         r.use_pdl = pdl;
         TRYCUDA(launch_rope_append(r, st), "rope/append");
         float *ctx_out = s->qmax ? s->d_ctx_pad + (size_t)s->rank * s->qmax * hd : s->d_ctx + (size_t)s->qa * hd;
@@ -171,11 +245,16 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
         TRY(session_exchange(s, s->d_hidden, (size_t)s->h0, (size_t)(s->h1 - s->h0), st));
         TRYCUDA(launch_rmsnorm(s->d_hidden, L.ffn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
         const int nf = s->f1 - s->f0;
-        TRY(run_gemv(s->ctx, L.gate.payload, nf, H, L.gate.format, SATORI_ORDER_BATCH, s->d_normed, s->d_gate, 1,
-                     kEpiNone, nullptr, nullptr, st, pdl));
-        TRY(run_gemv(s->ctx, L.up.payload, nf, H, L.up.format, SATORI_ORDER_BATCH, s->d_normed, s->d_up, 1, kEpiNone,
-                     nullptr, nullptr, st, pdl));
-        TRYCUDA(launch_swiglu(s->d_gate, s->d_up, nf, s->d_act + s->f0, st, pdl), "swiglu");
+        if (L.gu.payload) {
+            TRY(run_gemv(s->ctx, L.gu.payload, 2 * nf, H, L.gu.format, SATORI_ORDER_BATCH, s->d_normed,
+                         s->d_act + s->f0, 1, kEpiSwiGlu, nullptr, nullptr, st, pdl));
+        } else {
+            TRY(run_gemv(s->ctx, L.gate.payload, nf, H, L.gate.format, SATORI_ORDER_BATCH, s->d_normed, s->d_gate, 1,
+                         kEpiNone, nullptr, nullptr, st, pdl));
+            TRY(run_gemv(s->ctx, L.up.payload, nf, H, L.up.format, SATORI_ORDER_BATCH, s->d_normed, s->d_up, 1,
+                         kEpiNone, nullptr, nullptr, st, pdl));
+            TRYCUDA(launch_swiglu(s->d_gate, s->d_up, nf, s->d_act + s->f0, st, pdl), "swiglu");
+        }
         TRY(session_exchange(s, s->d_act, (size_t)s->f0, (size_t)nf, st));
         TRY(run_gemv(s->ctx, L.down.payload, s->h1 - s->h0, s->ffn, L.down.format, SATORI_ORDER_BATCH, s->d_act,
                      s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl));
@@ -185,7 +264,8 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
     TRY(run_gemv(s->ctx, s->output.payload, s->v1 - s->v0, H, s->output.format, SATORI_ORDER_BATCH, s->d_final,
                  s->d_logits + s->v0, 1, kEpiNone, nullptr, nullptr, st, pdl));
     TRY(session_exchange(s, s->d_logits, (size_t)s->v0, (size_t)(s->v1 - s->v0), st));
-    TRYCUDA(launch_argmax_advance(s->d_logits, s->vocab, s->d_argmax, s->d_nonfinite, s->d_pos, s->d_token, st, pdl),
+    TRYCUDA(launch_argmax_advance(s->d_logits, s->vocab, s->d_argmax, s->d_nonfinite, s->d_pos, s->d_token,
+                                  reinterpret_cast<unsigned *>(s->d_ints + 8), s->ctx->sm_count, st, pdl),
             "argmax");
     return SATORI_OK;
 }
@@ -234,6 +314,16 @@ static int session_upload(satori_session *s, const satori_model_desc *d)
         TRY(fetch_vector(s, d, p + "attn_q_norm.weight", s->head_dim, &L.q_norm, true));
         TRY(fetch_vector(s, d, p + "attn_k_norm.weight", s->head_dim, &L.k_norm, true));
         if (!!L.q_norm != !!L.k_norm) return set_error(SATORI_ERR_ARGUMENT, "layer %d has a partial q/k norm set", l);
+        if (s->fuse && L.q.format == L.k.format && L.q.format == L.v.format) {
+            TRY(combine_rows(s, {&L.q, &L.k, &L.v}, false, &L.qkv));
+            if (L.q_bias)
+                TRY(stack_vectors(s, {{&L.q_bias, s->q_local}, {&L.k_bias, s->kv_local}, {&L.v_bias, s->kv_local}},
+                                  &L.qkv_bias));
+        }
+        const int nf = s->f1 - s->f0;
+        if (s->fuse && L.gate.format == L.up.format &&
+            gemv_rows_takes(2 * nf, H, L.gate.format, s->ctx->sm_count, s->ctx->smem_optin))
+            TRY(combine_rows(s, {&L.gate, &L.up}, true, &L.gu));
     }
     const satori_tensor *e = find_tensor(d, "token_embd.weight");
     // GgufQuantizedMatrix.ReadRow rejects Q4_0 embedding rows (GgufQuantizedMatrix.cs:56).
@@ -266,14 +356,16 @@ int session_alloc_state(satori_session *s)
     TRY(dalloc(s, &s->d_normed, s->hidden));
     TRY(dalloc(s, &s->d_final, s->hidden));
     TRY(dalloc(s, &s->d_proj, s->hidden));
-    TRY(dalloc(s, &s->d_q, s->q_local));
+    TRY(dalloc(s, &s->d_qkv, (size_t)s->q_local + 2 * s->kv_local));
+    s->d_q = s->d_qkv;
+    s->d_k = s->d_qkv + s->q_local;
+    s->d_v = s->d_k + s->kv_local;
     TRY(dalloc(s, &s->d_qrot, s->q_local));
     if (s->qmax) TRY(dalloc(s, &s->d_ctx_pad, (size_t)s->world * s->qmax * s->head_dim));
-    TRY(dalloc(s, &s->d_k, s->kv_local));
-    TRY(dalloc(s, &s->d_v, s->kv_local));
     TRY(dalloc(s, &s->d_gate, s->f1 - s->f0));
     TRY(dalloc(s, &s->d_up, s->f1 - s->f0));
-    TRY(dalloc(s, &s->d_ints, 8));
+    TRY(dalloc(s, &s->d_ints, 12));   // 0-6 step state (read back), 8-11 argmax scratch
+    TRY(dalloc(s, &s->d_rope, (size_t)s->head_dim));
     s->d_token = s->d_ints + 0;
     s->d_pos = s->d_ints + 1;
     s->d_tokens = s->d_ints + 2;
@@ -317,6 +409,8 @@ satori_session *session_new(satori_ctx *ctx, const satori_model_desc *d, int con
     s->q_width = d->q_heads * d->head_dim;
     s->kv_width = d->kv_heads * d->head_dim;
     s->use_pdl = 1;
+    const char *fuse = getenv("SATORI_FUSE");
+    s->fuse = !(fuse && strcmp(fuse, "0") == 0);
     return s;
 }
 

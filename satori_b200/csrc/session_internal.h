@@ -29,6 +29,10 @@ struct Layer {
     float *q_bias = nullptr, *k_bias = nullptr, *v_bias = nullptr;
     float *q_norm = nullptr, *k_norm = nullptr;
     DevMatrix q, k, v, o, gate, up, down;
+    // Fused forms (when the formats agree): q, k, v rows stacked (one launch, biases stacked alike) and
+    // ffn_gate / ffn_up rows interleaved (one launch with the SwiGLU epilogue).  The parts are then freed.
+    DevMatrix qkv, gu;
+    float *qkv_bias = nullptr;
 };
 
 struct ShardState;  // multi-GPU exchange state (session_sharded.cu)
@@ -42,6 +46,7 @@ struct satori_session {
     int context = 0;
     int position = 0;
     int use_pdl = 1;
+    int fuse = 1;                    // stack q/k/v and interleave gate/up (SATORI_FUSE=0 keeps them apart)
     size_t weight_bytes = 0;
 
     std::vector<Layer> layer;
@@ -51,8 +56,10 @@ struct satori_session {
     float *d_kcache = nullptr, *d_vcache = nullptr;
     float *d_hidden = nullptr, *d_normed = nullptr, *d_final = nullptr, *d_proj = nullptr;
     float *d_q = nullptr, *d_qrot = nullptr, *d_ctx = nullptr, *d_k = nullptr, *d_v = nullptr;
+    float *d_qkv = nullptr;          // [q_local | kv_local | kv_local]: d_q, d_k, d_v point into it
     float *d_gate = nullptr, *d_up = nullptr, *d_act = nullptr, *d_logits = nullptr;
     float *d_attn_scratch = nullptr;
+    double *d_rope = nullptr;        // this step's RoPE cos/sin per pair (written by the embed kernel)
     int *d_ints = nullptr;
     int *d_token = nullptr, *d_pos = nullptr, *d_tokens = nullptr, *d_argmax = nullptr, *d_nonfinite = nullptr;
     int *h_ints = nullptr;

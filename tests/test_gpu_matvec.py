@@ -107,6 +107,24 @@ def test_baseline_shapes_bit_exact(sat, ctx, oracle_lib, fmt, rows, cols):
     _assert_exact(m.execute(x), oracle_lib.q_matvec(payload, rows, cols, fmt, x, order="avx2", threads=8), "execute")
 
 
+@pytest.mark.parametrize("fmt,rows,cols", [(0, 3, 8448), (1, 500, 8960), (0, 1536, 8960), (1, 37, 12288),
+                                           (0, 61, 12544), (1, 3584, 18944), (0, 100, 24576), (1, 29, 24832)])
+def test_decode_order_row_widths_bit_exact(sat, ctx, oracle_lib, fmt, rows, cols):
+    """ExecuteBatch at one position across the widths that pick each decode kernel shape (one or two
+    block columns per lane, 8 or 12 compute warps, and the column-chunked kernel past 24576)."""
+    rng = np.random.default_rng(rows + cols + fmt)
+    bb = 34 if fmt == 0 else 18
+    payload = rng.integers(0, 256, size=rows * (cols // 32) * bb, dtype=np.uint8)
+    scales = (rng.standard_normal(rows * (cols // 32)) * 0.05).astype(np.float16).view(np.uint16)
+    p2 = payload.reshape(-1, bb)
+    p2[:, 0] = scales & 0xFF
+    p2[:, 1] = scales >> 8
+    x = rng.standard_normal(cols).astype(np.float32)
+    m = sat.CudaMatrixFactory(ctx).create(payload, sat.QuantizedMatrixShape(rows, cols, fmt))
+    _assert_exact(m.execute_batch(x, 1), oracle_lib.q_matvec(payload, rows, cols, fmt, x, order="batch", threads=8),
+                  "batch")
+
+
 @pytest.mark.parametrize("positions", [2, 3, 8, 11])
 def test_batch_positions_bit_exact(sat, ctx, oracle_lib, positions):
     """ExecuteBatch with several positions: each position's rows equal the reference's."""

@@ -115,3 +115,20 @@ def test_qwen2_1_5b_shape_greedy_tokens_identical(sat, ctx, oracle_lib):
     spec = sat.qwen2_1_5b()
     prompt = list(np.random.default_rng(4).integers(0, spec.vocab, 12))
     _run_pair(sat, ctx, spec, prompt=prompt, n_gen=12, context=32, seed=21)
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_fused_projections_match_separate_launches_bitwise(sat, ctx, oracle_lib, fmt, monkeypatch):
+    """q/k/v stacked into one launch and gate/up interleaved with the SwiGLU epilogue give the same
+    bits as the separate launches (each row keeps its own FP32 chain; SwiGLU is the same function)."""
+    spec = sat.tiny(proj_format=fmt)           # hidden 256: the gate/up pair takes the fused epilogue
+    tensors = synthetic_tensors(spec, 9)
+    fused = sat.CudaDenseSession(spec, tensors, 32, ctx=ctx)
+    monkeypatch.setenv("SATORI_FUSE", "0")
+    apart = sat.CudaDenseSession(spec, tensors, 32, ctx=ctx)
+    t = 5
+    for _ in range(12):
+        a, ta = fused.append(t)
+        b, tb = apart.append(t)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)) and ta == tb
+        t = ta
