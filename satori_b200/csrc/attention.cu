@@ -37,7 +37,7 @@ struct AttnParams {
     const int *tokens_dev;
     int nsplit;
     float scale;
-    float *scratch;
+    float *scratch;        // split records [nsplit][q_heads][head_dim + 2]
     float *out;
     unsigned *err;
     int use_pdl;
@@ -99,7 +99,10 @@ __global__ void __launch_bounds__(kWarps * 32) attn_partial_kernel(AttnParams p)
     const int kvw = p.kv_stride;
     const int hl = lane / R;
 
-    if (p.use_pdl) pdl_wait();
+    if (p.use_pdl) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
     const int T = p.tokens_dev ? *p.tokens_dev : p.tokens;
     const int t0 = (int)(((long long)T * split) / p.nsplit);
     const int t1 = (int)(((long long)T * (split + 1)) / p.nsplit);
@@ -217,7 +220,73 @@ __global__ void __launch_bounds__(kWarps * 32) attn_partial_kernel(AttnParams p)
         }
         p.scratch[((long long)split * p.q_heads + h0 + h) * rec_stride + e] = val;
     }
-    if (p.use_pdl) pdl_launch_dependents();
+}
+
+// FP64 recompute of one head (the reference's arithmetic), used when FP32 scores overflowed.
+__device__ void head_fp64(const AttnParams &p, int head, int T, double *sbuf, float *out)
+{
+    const int hd = p.head_dim, kvw = p.kv_stride;
+    const int kvh = head / p.group;
+    const float *q = p.q + (long long)head * hd;
+    const double scale = 1.0 / sqrt((double)hd);
+    __shared__ double red[128];
+    // pass 1: max score
+    double mx = -INFINITY;
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const float *k = p.keys + (long long)t * kvw + kvh * hd;
+        double dot = 0;
+        for (int j = 0; j < hd; ++j) dot = __dadd_rn(dot, __dmul_rn((double)q[j], (double)k[j]));
+        mx = fmax(mx, __dmul_rn(dot, scale));
+    }
+    red[threadIdx.x] = mx;
+    __syncthreads();
+    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+        if (threadIdx.x < s) red[threadIdx.x] = fmax(red[threadIdx.x], red[threadIdx.x + s]);
+        __syncthreads();
+    }
+    mx = red[0];
+    __syncthreads();
+    // pass 2: total
+    double tot = 0;
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const float *k = p.keys + (long long)t * kvw + kvh * hd;
+        double dot = 0;
+        for (int j = 0; j < hd; ++j) dot = __dadd_rn(dot, __dmul_rn((double)q[j], (double)k[j]));
+        tot = __dadd_rn(tot, exp(__dsub_rn(__dmul_rn(dot, scale), mx)));
+    }
+    red[threadIdx.x] = tot;
+    __syncthreads();
+    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+        if (threadIdx.x < s) red[threadIdx.x] = __dadd_rn(red[threadIdx.x], red[threadIdx.x + s]);
+        __syncthreads();
+    }
+    tot = red[0];
+    __syncthreads();
+    // pass 3: sum_t (p_t / total) * v_t, in token order per dim
+    double sum[2] = {0, 0};
+    for (int tc = 0; tc < T; tc += blockDim.x) {
+        const int t = tc + threadIdx.x;
+        if (t < T) {
+            const float *k = p.keys + (long long)t * kvw + kvh * hd;
+            double dot = 0;
+            for (int j = 0; j < hd; ++j) dot = __dadd_rn(dot, __dmul_rn((double)q[j], (double)k[j]));
+            sbuf[threadIdx.x] = exp(__dsub_rn(__dmul_rn(dot, scale), mx));
+        }
+        __syncthreads();
+        const int n = min((int)blockDim.x, T - tc);
+        for (int r = 0; r < 2; ++r) {
+            const int d = threadIdx.x + r * blockDim.x;
+            if (d < hd)
+                for (int j = 0; j < n; ++j)
+                    sum[r] = __dadd_rn(sum[r], __dmul_rn(__ddiv_rn(sbuf[j], tot),
+                                                         (double)p.values[(long long)(tc + j) * kvw + kvh * hd + d]));
+        }
+        __syncthreads();
+    }
+    for (int r = 0; r < 2; ++r) {
+        const int d = threadIdx.x + r * blockDim.x;
+        if (d < hd) out[d] = (float)sum[r];
+    }
 }
 
 // Streaming variant for head_dim 128 and groups of up to 8 query heads (every BASELINE shape):
@@ -272,7 +341,10 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
         fence_mbar_init();
     }
     __syncthreads();
-    if (p.use_pdl) pdl_wait();   // the token count and the newest K/V row come from earlier kernels
+    if (p.use_pdl) {   // the token count and the newest K/V row come from earlier kernels
+        pdl_launch_dependents();
+        pdl_wait();
+    }
     const int T = p.tokens_dev ? *p.tokens_dev : p.tokens;
     const int t0 = (int)(((long long)T * split) / p.nsplit);
     const int t1 = (int)(((long long)T * (split + 1)) / p.nsplit);
@@ -420,74 +492,6 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
         }
         p.scratch[((long long)split * p.q_heads + h0 + h) * rec_stride + e] = val;
     }
-    if (p.use_pdl) pdl_launch_dependents();
-}
-
-// FP64 recompute of one head (the reference's arithmetic), used when FP32 scores overflowed.
-__device__ void head_fp64(const AttnParams &p, int head, int T, double *sbuf, float *out)
-{
-    const int hd = p.head_dim, kvw = p.kv_stride;
-    const int kvh = head / p.group;
-    const float *q = p.q + (long long)head * hd;
-    const double scale = 1.0 / sqrt((double)hd);
-    __shared__ double red[128];
-    // pass 1: max score
-    double mx = -INFINITY;
-    for (int t = threadIdx.x; t < T; t += blockDim.x) {
-        const float *k = p.keys + (long long)t * kvw + kvh * hd;
-        double dot = 0;
-        for (int j = 0; j < hd; ++j) dot = __dadd_rn(dot, __dmul_rn((double)q[j], (double)k[j]));
-        mx = fmax(mx, __dmul_rn(dot, scale));
-    }
-    red[threadIdx.x] = mx;
-    __syncthreads();
-    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
-        if (threadIdx.x < s) red[threadIdx.x] = fmax(red[threadIdx.x], red[threadIdx.x + s]);
-        __syncthreads();
-    }
-    mx = red[0];
-    __syncthreads();
-    // pass 2: total
-    double tot = 0;
-    for (int t = threadIdx.x; t < T; t += blockDim.x) {
-        const float *k = p.keys + (long long)t * kvw + kvh * hd;
-        double dot = 0;
-        for (int j = 0; j < hd; ++j) dot = __dadd_rn(dot, __dmul_rn((double)q[j], (double)k[j]));
-        tot = __dadd_rn(tot, exp(__dsub_rn(__dmul_rn(dot, scale), mx)));
-    }
-    red[threadIdx.x] = tot;
-    __syncthreads();
-    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
-        if (threadIdx.x < s) red[threadIdx.x] = __dadd_rn(red[threadIdx.x], red[threadIdx.x + s]);
-        __syncthreads();
-    }
-    tot = red[0];
-    __syncthreads();
-    // pass 3: sum_t (p_t / total) * v_t, in token order per dim
-    double sum[2] = {0, 0};
-    for (int tc = 0; tc < T; tc += blockDim.x) {
-        const int t = tc + threadIdx.x;
-        if (t < T) {
-            const float *k = p.keys + (long long)t * kvw + kvh * hd;
-            double dot = 0;
-            for (int j = 0; j < hd; ++j) dot = __dadd_rn(dot, __dmul_rn((double)q[j], (double)k[j]));
-            sbuf[threadIdx.x] = exp(__dsub_rn(__dmul_rn(dot, scale), mx));
-        }
-        __syncthreads();
-        const int n = min((int)blockDim.x, T - tc);
-        for (int r = 0; r < 2; ++r) {
-            const int d = threadIdx.x + r * blockDim.x;
-            if (d < hd)
-                for (int j = 0; j < n; ++j)
-                    sum[r] = __dadd_rn(sum[r], __dmul_rn(__ddiv_rn(sbuf[j], tot),
-                                                         (double)p.values[(long long)(tc + j) * kvw + kvh * hd + d]));
-        }
-        __syncthreads();
-    }
-    for (int r = 0; r < 2; ++r) {
-        const int d = threadIdx.x + r * blockDim.x;
-        if (d < hd) out[d] = (float)sum[r];
-    }
 }
 
 __global__ void __launch_bounds__(128) attn_merge_kernel(AttnParams p)
@@ -497,7 +501,10 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(AttnParams p)
     __shared__ double sbuf[128];
     const int head = blockIdx.x;
     const int hd = p.head_dim, rs = hd + 2;
-    if (p.use_pdl) pdl_wait();
+    if (p.use_pdl) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
     if (threadIdx.x == 0) bad = 0;
     __syncthreads();
     const float *rec = p.scratch + (long long)head * rs;
@@ -536,7 +543,6 @@ __global__ void __launch_bounds__(128) attn_merge_kernel(AttnParams p)
             if (d < hd) p.out[(long long)head * hd + d] = o[r];
         }
     }
-    if (p.use_pdl) pdl_launch_dependents();
 }
 
 template <int DPL, bool VEC4, int GMAX>
@@ -570,7 +576,10 @@ int gmax_for(int group) { return group >= 8 ? 8 : group > 2 ? (group > 4 ? 8 : 4
 // ---------------------------------------------------------------- RoPE + append
 __global__ void rope_append_kernel(RopeAppendArgs a)
 {
-    if (a.use_pdl) pdl_wait();
+    if (a.use_pdl) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
     const int pos = a.position_dev ? *a.position_dev : a.position;
     const int hd = a.head_dim, half = a.rotary / 2;
     const int qw = a.q_heads * hd, kvw = a.kv_heads * hd;
@@ -607,7 +616,6 @@ __global__ void rope_append_kernel(RopeAppendArgs a)
             vslot[e] = a.v[e];
         }
     }
-    if (a.use_pdl) pdl_launch_dependents();
 }
 
 __global__ void rope_half_kernel(float *v, int n, int hd, int pos, double base, int rotary)

@@ -115,7 +115,7 @@ int upload_payload(satori_ctx *ctx, const uint8_t *src, bool src_is_device, size
 
 int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int format, int order, const float *dx,
              float *dy, int positions, int epilogue, const float *bias, float *residual, cudaStream_t stream,
-             int use_pdl)
+             int use_pdl, const float *norm_w, float norm_eps)
 {
     const int per_launch = order == SATORI_ORDER_BATCH ? 8 : 1;
     for (int p0 = 0; p0 < positions; p0 += per_launch) {
@@ -136,12 +136,15 @@ int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int 
             a.residual = residual;
             a.err = ctx->d_err;
             a.use_pdl = use_pdl;
+            a.norm_w = norm_w;
+            a.norm_eps = norm_eps;
             DecodePlan dp = plan_gemv_rows(a, ctx->sm_count, ctx->smem_optin);
             if (dp.ok) {
                 cudaError_t e = launch_gemv_rows(a, dp, stream);
                 if (e != cudaSuccess) return cuda_fail(e, "launch decode MatVec");
                 continue;
             }
+            if (norm_w) return set_error(SATORI_ERR_NOT_SUPPORTED, "the fused RmsNorm needs the decode rows kernel");
             dp = plan_gemv_decode(a, ctx->sm_count, ctx->smem_optin);
             if (dp.ok) {
                 cudaError_t e = launch_gemv_decode(a, dp, stream);
@@ -149,8 +152,8 @@ int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int 
                 continue;
             }
         }
-        if (epilogue == kEpiSwiGlu)
-            return set_error(SATORI_ERR_NOT_SUPPORTED, "the fused SwiGLU epilogue needs the decode rows kernel");
+        if (epilogue == kEpiSwiGlu || norm_w)
+            return set_error(SATORI_ERR_NOT_SUPPORTED, "fused SwiGLU / RmsNorm need the decode rows kernel");
         GemvPlan plan = plan_gemv(rows, cols, format, np, ctx->sm_count, ctx->smem_optin);
         if (!plan.ok) return set_error(SATORI_ERR_ARGUMENT, "no MatVec plan fits shared memory for %dx%d", rows, cols);
         GemvArgs a = {};
@@ -464,6 +467,7 @@ static int ensure_attn_scratch(satori_ctx *ctx, size_t floats)
     ctx->attn_scratch_floats = 0;
     cudaError_t e = cudaMalloc(&ctx->attn_scratch, floats * 4);
     if (e != cudaSuccess) return cuda_fail(e, "allocate attention scratch");
+
     ctx->attn_scratch_floats = floats;
     return SATORI_OK;
 }
@@ -489,6 +493,7 @@ extern "C" int satori_grouped_attention_device(satori_ctx *ctx, const float *q, 
     a.out = out;
     a.scratch = ctx->attn_scratch;
     a.err = ctx->d_err;
+    a.use_pdl = 1;
     cudaError_t e = launch_attention(a, ctx->sm_count, ctx->stream);
     return e == cudaSuccess ? SATORI_OK : cuda_fail(e, "launch attention");
 }

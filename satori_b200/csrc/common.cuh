@@ -43,6 +43,34 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t bits16)
     return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFFu)));
 }
 
+// TransformerOps.RmsNorm's sum of squares (TransformerOps.cs:13-22) in FP64, in one fixed order that
+// every kernel uses, so a norm fused into a MatVec equals the standalone norm kernel bit for bit:
+// 256 strided partials (partial j adds x[j]^2, x[j+256]^2, ... in index order), a shuffle-xor tree over
+// each warp's 32 partials, then ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)).  Threads 0..255 of the block call
+// rms_partial (warp w's lane 0 stores s_w into red[w]); after a barrier any thread calls rms_scale.
+__device__ __forceinline__ void rms_partial(const float *x, int n, int tid, double *red)
+{
+    double sum = 0;
+    for (int i = tid; i < n; i += 256) sum = __dadd_rn(sum, __dmul_rn((double)x[i], (double)x[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum = __dadd_rn(sum, __shfl_xor_sync(0xFFFFFFFFu, sum, o));
+    if ((tid & 31) == 0) red[tid >> 5] = sum;
+}
+
+// 1 / sqrt(sum / n + eps), the RmsNorm scale, from the eight warp sums.
+__device__ __forceinline__ double rms_scale(const double *red, int n, float eps)
+{
+    const double sum = __dadd_rn(__dadd_rn(__dadd_rn(red[0], red[1]), __dadd_rn(red[2], red[3])),
+                                 __dadd_rn(__dadd_rn(red[4], red[5]), __dadd_rn(red[6], red[7])));
+    return __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)n), (double)eps)));
+}
+
+// One normalised element: (float)(x * scale * w), each product rounded in FP64.
+__device__ __forceinline__ float rms_apply(float x, double scale, float w)
+{
+    return (float)__dmul_rn(__dmul_rn((double)x, scale), (double)w);
+}
+
 // TransformerOps.SwiGlu (TransformerOps.cs:41-51) for one element: FP64 sigmoid of the gate, every
 // multiply and add rounded separately, FP32 result.
 __device__ __forceinline__ float swiglu_value(float gate, float up)

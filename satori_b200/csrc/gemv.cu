@@ -321,7 +321,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(Geo g)
     if (warp == 7)
         for (int c = 0; c < min(S, g.nchunks); ++c) issue_chunk(c);
 
-    if (g.use_pdl) pdl_wait();
+    if (g.use_pdl) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
 
     // Stage the activation vector(s), swizzled.
     for (int p = 0; p < g.P; ++p) {
@@ -410,7 +413,6 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(Geo g)
         if (warp == 7 && c < g.nchunks && c + S < g.nchunks) issue_chunk(c + S);
     }
 
-    if (g.use_pdl) pdl_launch_dependents();
 
     if (is_chain && chain_row < RC && !abort_flag) {
         const int row = r0 + chain_row;

@@ -27,6 +27,8 @@ struct GemvArgs {
     float *residual;         // [rows] for kEpiResidual (positions == 1)
     unsigned *err;           // device error word
     int use_pdl;             // launched with programmatic stream serialization
+    const float *norm_w;     // non-null: x is RmsNorm'ed on the fly with these weights (gemv_rows only)
+    float norm_eps;
 };
 
 // Geometry the host chooses for one launch.
@@ -47,8 +49,9 @@ struct DecodePlan {
     size_t smem;
 };
 DecodePlan plan_gemv_rows(const GemvArgs &a, int sm_count, size_t smem_limit);
-// True when the decode-order rows kernel takes this shape (and so the fused SwiGLU epilogue).
-bool gemv_rows_takes(int rows, int cols, int format, int sm_count, size_t smem_limit);
+// True when the decode-order rows kernel takes this shape with this epilogue (and so the fused SwiGLU
+// epilogue and the fused RmsNorm of x).
+bool gemv_rows_takes(int rows, int cols, int format, int epilogue, int sm_count, size_t smem_limit);
 cudaError_t launch_gemv_rows(const GemvArgs &a, const DecodePlan &plan, cudaStream_t stream);
 DecodePlan plan_gemv_decode(const GemvArgs &a, int sm_count, size_t smem_limit);
 cudaError_t launch_gemv_decode(const GemvArgs &a, const DecodePlan &plan, cudaStream_t stream);

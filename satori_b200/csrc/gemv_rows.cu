@@ -62,6 +62,8 @@ struct RowsGeo {
     float *residual;
     unsigned *err;
     int use_pdl;
+    const float *norm_w;  // non-null: RmsNorm x (TransformerOps.RmsNorm) before the products
+    float norm_eps;
 };
 
 // Bounded wait until a shared counter reaches `target` (written by the control warp).
@@ -91,6 +93,7 @@ __device__ __forceinline__ void rows_load(const uint8_t *a, uint32_t (&w)[9])
 struct RowsHeader {
     uint64_t *full, *empty, *dfull;
     volatile int *abort_flag, *folded;   // folded = fold batches whose rows are written out
+    double *red;                         // the RmsNorm's eight warp sums
     __device__ explicit RowsHeader(uint8_t *smem)
     {
         full = reinterpret_cast<uint64_t *>(smem);
@@ -98,8 +101,10 @@ struct RowsHeader {
         dfull = empty + kRowsMaxStages;
         abort_flag = reinterpret_cast<volatile int *>(dfull + kFoldSlots);
         folded = abort_flag + 1;
+        red = reinterpret_cast<double *>(dfull + kFoldSlots + 1);
     }
 };
+static_assert((2 * kRowsMaxStages + kFoldSlots + 1 + 8) * 8 <= kRowsHeader, "rows header");
 
 // The compute-warp side for one phase (PH = byte offset of the lane's blocks inside their first word).
 // A lane owns NB block columns of its phase: e_k = (k * wpp + column warp) * 32 + lane.
@@ -118,6 +123,7 @@ __device__ __forceinline__ bool rows_compute(const RowsGeo &g, uint8_t *smem, in
     bool valid[NB];
     uint32_t wofs[NB];                                 // byte offset of the word holding the block's first byte
     float4 xv[NB][8];
+    const double scale = g.norm_w ? rms_scale(h.red, g.bpr * 32, g.norm_eps) : 0.0;
 #pragma unroll
     for (int k = 0; k < NB; ++k) {
         e[k] = (k * g.wpp + cw) * 32 + lane;
@@ -127,6 +133,15 @@ __device__ __forceinline__ bool rows_compute(const RowsGeo &g, uint8_t *smem, in
         const float4 *xb = reinterpret_cast<const float4 *>(g.x) + (size_t)b * 8;
 #pragma unroll
         for (int q = 0; q < 8; ++q) xv[k][q] = xb[q];
+        if (g.norm_w) {
+            const float4 *wb = reinterpret_cast<const float4 *>(g.norm_w) + (size_t)b * 8;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 w4 = wb[q];
+                xv[k][q] = make_float4(rms_apply(xv[k][q].x, scale, w4.x), rms_apply(xv[k][q].y, scale, w4.y),
+                                       rms_apply(xv[k][q].z, scale, w4.z), rms_apply(xv[k][q].w, scale, w4.w));
+            }
+        }
     }
 
     int dcol[NB];                                      // the lane's columns in a term-table row
@@ -252,6 +267,11 @@ __global__ void __launch_bounds__(rows_threads(CW), CW == 8 ? 2 : 1) gemv_rows_k
     if (g.use_pdl) {
         pdl_launch_dependents();
         pdl_wait();
+    }
+    if (g.norm_w) {
+        // The RmsNorm scale of x: warps 0..7 form the fixed-order sum, every thread reads it back.
+        if (tid < 256) rms_partial(g.x, g.bpr * 32, tid, h.red);
+        __syncthreads();
     }
 
     if (producer) {
@@ -437,7 +457,7 @@ DecodePlan plan_gemv_rows(const GemvArgs &a, int sm_count, size_t smem_limit)
     return p;
 }
 
-bool gemv_rows_takes(int rows, int cols, int format, int sm_count, size_t smem_limit)
+bool gemv_rows_takes(int rows, int cols, int format, int epilogue, int sm_count, size_t smem_limit)
 {
     GemvArgs a = {};
     a.rows = rows;
@@ -445,7 +465,7 @@ bool gemv_rows_takes(int rows, int cols, int format, int sm_count, size_t smem_l
     a.format = format;
     a.order = SATORI_ORDER_BATCH;
     a.positions = 1;
-    a.epilogue = kEpiSwiGlu;
+    a.epilogue = epilogue;
     // Device allocations and the session's vectors are 256-byte aligned; stand-ins with that alignment.
     a.payload = reinterpret_cast<const uint8_t *>(uintptr_t(256));
     a.x = reinterpret_cast<const float *>(uintptr_t(256));
@@ -482,6 +502,8 @@ cudaError_t launch_gemv_rows(const GemvArgs &a, const DecodePlan &plan, cudaStre
     g.residual = a.residual;
     g.err = a.err;
     g.use_pdl = a.use_pdl;
+    g.norm_w = a.norm_w;
+    g.norm_eps = a.norm_eps;
     const bool q8 = a.format == 0;
     if (plan.nb == 2) return q8 ? launch_rows<0, 12, 2>(g, plan, stream) : launch_rows<1, 12, 2>(g, plan, stream);
     switch (plan.cw) {

@@ -38,24 +38,27 @@ __device__ double block_sum_double(double v, double *red)
     return r;
 }
 
-__global__ void __launch_bounds__(1024) rmsnorm_kernel(const float *x, const float *w, int n, float eps, float *out,
-                                                       int pdl)
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const float *w, int n, float eps, float *out,
+                                                      int pdl)
 {
-    __shared__ double red[1024];
-    if (pdl) pdl_wait();
-    double sum = 0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) sum = __dadd_rn(sum, __dmul_rn((double)x[i], (double)x[i]));
-    sum = block_sum_double(sum, red);
-    const double scale = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)n), (double)eps)));
-    for (int i = threadIdx.x; i < n; i += blockDim.x)
-        out[i] = (float)__dmul_rn(__dmul_rn((double)x[i], scale), (double)w[i]);
-    if (pdl) pdl_launch_dependents();
+    __shared__ double red[8];
+    if (pdl) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
+    rms_partial(x, n, threadIdx.x, red);
+    __syncthreads();
+    const double scale = rms_scale(red, n, eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = rms_apply(x[i], scale, w[i]);
 }
 
 __global__ void rmsnorm_heads_kernel(float *v, int n, const float *w, float eps, int hd, int pdl)
 {
     __shared__ double red[128];
-    if (pdl) pdl_wait();
+    if (pdl) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
     float *h = v + (long long)blockIdx.x * hd;
     double sum = 0;
     for (int i = threadIdx.x; i < hd; i += blockDim.x) sum = __dadd_rn(sum, __dmul_rn((double)h[i], (double)h[i]));
@@ -63,21 +66,25 @@ __global__ void rmsnorm_heads_kernel(float *v, int n, const float *w, float eps,
     const double scale = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)hd), (double)eps)));
     for (int i = threadIdx.x; i < hd; i += blockDim.x)
         h[i] = (float)__dmul_rn(__dmul_rn((double)h[i], scale), (double)w[i]);
-    if (pdl) pdl_launch_dependents();
 }
 
 __global__ void swiglu_kernel(const float *gate, const float *up, int n, float *out, int pdl)
 {
-    if (pdl) pdl_wait();
+    if (pdl) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
         out[i] = swiglu_value(gate[i], up[i]);
-    if (pdl) pdl_launch_dependents();
 }
 
 __global__ void embed_kernel(const uint8_t *embd, int cols, const int *token_dev, const int *pos_dev, int *tokens_dev,
                              float *hidden, double *rope_table, double rope_base, int rotary, int pdl)
 {
-    if (pdl) pdl_wait();
+    if (pdl) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
     if (rope_table) {
         // TransformerOps.RopeHalf (TransformerOps.cs:99-118): the FP64 angle of pair k and its sin/cos,
         // the same for every head and layer of this step.
@@ -100,7 +107,6 @@ __global__ void embed_kernel(const uint8_t *embd, int cols, const int *token_dev
         hidden[i] = fmul(d, code);  // QuantizedRow.DecodeQ8Block
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) *tokens_dev = *pos_dev + 1;
-    if (pdl) pdl_launch_dependents();
 }
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, int idx)
@@ -122,7 +128,10 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float *log
     __shared__ unsigned long long red[kArgmaxThreads / 32];
     unsigned long long *best_dev = reinterpret_cast<unsigned long long *>(scratch);
     unsigned *ticket = scratch + 2;
-    if (pdl) pdl_wait();
+    if (pdl) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
     unsigned long long best = 0;
     bool bad = false;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -156,7 +165,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float *log
 
 cudaError_t launch_rmsnorm(const float *x, const float *w, int n, float eps, float *out, cudaStream_t s, int pdl)
 {
-    return launch_ex(rmsnorm_kernel, dim3(1), dim3(1024), 0, s, pdl, x, w, n, eps, out, pdl);
+    return launch_ex(rmsnorm_kernel, dim3(1), dim3(256), 0, s, pdl, x, w, n, eps, out, pdl);
 }
 
 cudaError_t launch_rmsnorm_heads(float *v, int n, const float *w, float eps, int head_dim, cudaStream_t s, int pdl)

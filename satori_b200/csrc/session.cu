@@ -179,10 +179,11 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
             "embed");
     for (int l = 0; l < s->layers; ++l) {
         const Layer &L = s->layer[l];
-        TRYCUDA(launch_rmsnorm(s->d_hidden, L.attn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
+        if (!L.qkv_norm) TRYCUDA(launch_rmsnorm(s->d_hidden, L.attn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
         if (L.qkv.payload) {
-            TRY(run_gemv(s->ctx, L.qkv.payload, L.qkv.rows, H, L.qkv.format, SATORI_ORDER_BATCH, s->d_normed, s->d_qkv,
-                         1, L.qkv_bias ? kEpiBias : kEpiNone, L.qkv_bias, nullptr, st, pdl));
+            TRY(run_gemv(s->ctx, L.qkv.payload, L.qkv.rows, H, L.qkv.format, SATORI_ORDER_BATCH,
+                         L.qkv_norm ? s->d_hidden : s->d_normed, s->d_qkv, 1, L.qkv_bias ? kEpiBias : kEpiNone,
+                         L.qkv_bias, nullptr, st, pdl, L.qkv_norm ? L.attn_norm : nullptr, s->eps));
         } else {
             TRY(run_gemv(s->ctx, L.q.payload, L.q.rows, H, L.q.format, SATORI_ORDER_BATCH, s->d_normed, s->d_q, 1,
                          L.q_bias ? kEpiBias : kEpiNone, L.q_bias, nullptr, st, pdl));
@@ -243,12 +244,13 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
         TRY(run_gemv(s->ctx, L.o.payload, s->h1 - s->h0, qw, L.o.format, SATORI_ORDER_BATCH, s->d_ctx,
                      s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl));
         TRY(session_exchange(s, s->d_hidden, (size_t)s->h0, (size_t)(s->h1 - s->h0), st));
-        TRYCUDA(launch_rmsnorm(s->d_hidden, L.ffn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
         const int nf = s->f1 - s->f0;
         if (L.gu.payload) {
-            TRY(run_gemv(s->ctx, L.gu.payload, 2 * nf, H, L.gu.format, SATORI_ORDER_BATCH, s->d_normed,
-                         s->d_act + s->f0, 1, kEpiSwiGlu, nullptr, nullptr, st, pdl));
+            // ffn_norm runs inside the launch: every CTA forms the same norm of the residual.
+            TRY(run_gemv(s->ctx, L.gu.payload, 2 * nf, H, L.gu.format, SATORI_ORDER_BATCH, s->d_hidden,
+                         s->d_act + s->f0, 1, kEpiSwiGlu, nullptr, nullptr, st, pdl, L.ffn_norm, s->eps));
         } else {
+            TRYCUDA(launch_rmsnorm(s->d_hidden, L.ffn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
             TRY(run_gemv(s->ctx, L.gate.payload, nf, H, L.gate.format, SATORI_ORDER_BATCH, s->d_normed, s->d_gate, 1,
                          kEpiNone, nullptr, nullptr, st, pdl));
             TRY(run_gemv(s->ctx, L.up.payload, nf, H, L.up.format, SATORI_ORDER_BATCH, s->d_normed, s->d_up, 1,
@@ -319,10 +321,12 @@ static int session_upload(satori_session *s, const satori_model_desc *d)
             if (L.q_bias)
                 TRY(stack_vectors(s, {{&L.q_bias, s->q_local}, {&L.k_bias, s->kv_local}, {&L.v_bias, s->kv_local}},
                                   &L.qkv_bias));
+            L.qkv_norm = gemv_rows_takes(L.qkv.rows, H, L.qkv.format, L.qkv_bias ? kEpiBias : kEpiNone,
+                                         s->ctx->sm_count, s->ctx->smem_optin);
         }
         const int nf = s->f1 - s->f0;
         if (s->fuse && L.gate.format == L.up.format &&
-            gemv_rows_takes(2 * nf, H, L.gate.format, s->ctx->sm_count, s->ctx->smem_optin))
+            gemv_rows_takes(2 * nf, H, L.gate.format, kEpiSwiGlu, s->ctx->sm_count, s->ctx->smem_optin))
             TRY(combine_rows(s, {&L.gate, &L.up}, true, &L.gu));
     }
     const satori_tensor *e = find_tensor(d, "token_embd.weight");

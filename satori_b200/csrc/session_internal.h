@@ -33,6 +33,7 @@ struct Layer {
     // ffn_gate / ffn_up rows interleaved (one launch with the SwiGLU epilogue).  The parts are then freed.
     DevMatrix qkv, gu;
     float *qkv_bias = nullptr;
+    bool qkv_norm = false;           // attn_norm runs inside the q/k/v launch (the rows kernel takes it)
 };
 
 struct ShardState;  // multi-GPU exchange state (session_sharded.cu)

@@ -66,6 +66,21 @@ def test_extreme_values_take_the_fp64_path(sat, ctx):
     np.testing.assert_array_equal(out, np.array([3, 4], np.float32))
 
 
+def test_overflowing_head_in_the_streaming_kernel_takes_the_fp64_path(sat, ctx, oracle_lib):
+    """28/4 x 128 (the streaming kernel and its fused split merge): one head's FP32 scores overflow, so
+    that head is recomputed in FP64 inside the merging CTA; every head stays within tolerance."""
+    qh, kvh, hd, tokens = 28, 4, 128, 300
+    q = seeded_normal(41, qh * hd)
+    k = seeded_normal(42, tokens * kvh * hd)
+    v = seeded_normal(43, tokens * kvh * hd)
+    q[3 * hd:4 * hd] = 1e19                                # head 3 reads KV head 0
+    k[(5 * kvh + 0) * hd:(5 * kvh + 1) * hd] = 1e19        # token 5 of KV head 0: score ~1e39 overflows
+    gpu = sat.TransformerOps.grouped_attention(q, k, v, qh, kvh, hd, tokens, ctx=ctx)
+    ref = oracle_lib.grouped_attention(q, k, v, qh, kvh, hd, tokens, threads=8)
+    _close(gpu, ref, "overflow")
+    np.testing.assert_allclose(gpu[3 * hd:4 * hd], v[(5 * kvh) * hd:(5 * kvh + 1) * hd], rtol=1e-6)
+
+
 def test_equal_heads_equals_mha_bitwise(sat, ctx):
     """QwenOperatorTests.cs:45-60."""
     rng = np.random.default_rng(11)
