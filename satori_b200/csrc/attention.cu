@@ -494,52 +494,86 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
     }
 }
 
-__global__ void __launch_bounds__(128) attn_merge_kernel(AttnParams p)
+// Split records are merged in chunks staged through shared memory with cp.async, so every record
+// load of a chunk is in flight at once (a thread walking the splits one global load at a time is
+// latency-bound).  The arithmetic and its order are unchanged: max over splits, then l and each output
+// dim as sequential fmaf sums over the splits in split order.
+constexpr int kMergeThreads = 128;
+constexpr int kMergeChunk = 32;   // splits staged per round
+
+__device__ __forceinline__ void cp_async4(float *dst, const float *src)
 {
-    extern __shared__ float wts[];  // [nsplit]
-    __shared__ int bad;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+__global__ void __launch_bounds__(kMergeThreads) attn_merge_kernel(AttnParams p)
+{
+    extern __shared__ float msm[];   // wts[nsplit] (padded to 4), then chunk[kMergeChunk][head_dim + 2]
+    __shared__ float wmax[kMergeThreads / 32];
     __shared__ double sbuf[128];
-    const int head = blockIdx.x;
+    const int head = blockIdx.x, tid = threadIdx.x;
     const int hd = p.head_dim, rs = hd + 2;
+    float *wts = msm;
+    float *chunk = msm + ((p.nsplit + 3) & ~3);
     if (p.use_pdl) {
         pdl_launch_dependents();
         pdl_wait();
     }
-    if (threadIdx.x == 0) bad = 0;
-    __syncthreads();
+    bool bad = false;   // this thread's view; combined before the result is written
     const float *rec = p.scratch + (long long)head * rs;
     const long long split_stride = (long long)p.q_heads * rs;
+    // Maximum of the split maxima (order-free), each split's max read by one thread.
     float m = -INFINITY;
-    for (int s = 0; s < p.nsplit; ++s) {
+    for (int s = tid; s < p.nsplit; s += kMergeThreads) {
         const float ms = rec[s * split_stride];
-        if (isnan(ms) || ms == INFINITY) bad = 1;
+        wts[s] = ms;
+        bad |= isnan(ms) || ms == INFINITY;
         m = fmaxf(m, ms);
     }
-    for (int s = threadIdx.x; s < p.nsplit; s += blockDim.x) {
-        const float ms = rec[s * split_stride];
-        wts[s] = ms == -INFINITY ? 0.0f : expf(ms - m);
-        if (!isfinite(rec[s * split_stride + 1])) bad = 1;
-    }
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if ((tid & 31) == 0) wmax[tid >> 5] = m;
     __syncthreads();
-    float l = 0.0f;
-    for (int s = 0; s < p.nsplit; ++s) l = fmaf(rec[s * split_stride + 1], wts[s], l);
-    float o[2] = {0.0f, 0.0f};
-    for (int r = 0; r < 2; ++r) {
-        const int d = threadIdx.x + r * blockDim.x;
-        if (d < hd) {
-            float a = 0.0f;
-            for (int s = 0; s < p.nsplit; ++s) a = fmaf(rec[s * split_stride + 2 + d], wts[s], a);
-            if (!isfinite(a)) bad = 1;
-            o[r] = a / l;
+    m = wmax[0];
+    for (int w = 1; w < kMergeThreads / 32; ++w) m = fmaxf(m, wmax[w]);
+    for (int s = tid; s < p.nsplit; s += kMergeThreads) {
+        const float ms = wts[s];
+        wts[s] = ms == -INFINITY ? 0.0f : expf(ms - m);
+    }
+    float l = 0.0f, a[2] = {0.0f, 0.0f};
+    for (int s0 = 0; s0 < p.nsplit; s0 += kMergeChunk) {
+        const int n = min(kMergeChunk, p.nsplit - s0);
+        __syncthreads();   // weights written; the previous chunk fully read
+        for (int i = tid; i < n * rs; i += kMergeThreads) {
+            const int s = i / rs, e = i - s * rs;
+            cp_async4(chunk + i, rec + (s0 + s) * split_stride + e);
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();
+        for (int s = 0; s < n; ++s) {
+            const float ls = chunk[s * rs + 1], w = wts[s0 + s];
+            bad |= !isfinite(ls);
+            l = fmaf(ls, w, l);
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int d = tid + r * kMergeThreads;
+                if (d < hd) a[r] = fmaf(chunk[s * rs + 2 + d], w, a[r]);
+            }
         }
     }
-    __syncthreads();
-    if (bad || !isfinite(l) || l <= 0.0f) {
+    float o[2] = {0.0f, 0.0f};
+    for (int r = 0; r < 2; ++r) {
+        const int d = tid + r * kMergeThreads;
+        if (d < hd) {
+            bad |= !isfinite(a[r]);
+            o[r] = a[r] / l;
+        }
+    }
+    if (__syncthreads_or(bad) || !isfinite(l) || l <= 0.0f) {
         const int T = p.tokens_dev ? *p.tokens_dev : p.tokens;
         head_fp64(p, head, T, sbuf, p.out + (long long)head * hd);
     } else {
         for (int r = 0; r < 2; ++r) {
-            const int d = threadIdx.x + r * blockDim.x;
+            const int d = tid + r * kMergeThreads;
             if (d < hd) p.out[(long long)head * hd + d] = o[r];
         }
     }
@@ -754,8 +788,13 @@ cudaError_t launch_attention(const AttnArgs &a, int sm_count, cudaStream_t strea
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.q_heads);
-    cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = sizeof(float) * (size_t)p.nsplit;
+    cfg.blockDim = dim3(kMergeThreads);
+    cfg.dynamicSmemBytes = sizeof(float) * ((size_t)((p.nsplit + 3) & ~3) + (size_t)kMergeChunk * (a.head_dim + 2));
+    if (cfg.dynamicSmemBytes > 48 * 1024) {
+        const cudaError_t ea = cudaFuncSetAttribute(attn_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    (int)cfg.dynamicSmemBytes);
+        if (ea != cudaSuccess) return ea;
+    }
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

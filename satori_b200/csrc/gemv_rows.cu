@@ -38,7 +38,7 @@ constexpr int kFoldSlots = 2;                          // term tables (fold batc
 constexpr int kRowsMaxStages = 16;
 constexpr int kRowsMaxStageRows = 32;                  // one control lane per row of a stage
 constexpr int kRowsHeader = 384;
-constexpr size_t kRowsStageTarget = 20 * 1024;         // bytes of weights per stage (narrow shape)
+constexpr size_t kRowsStageTarget = 40 * 1024;         // bytes of weights per stage (narrow shape)
 constexpr size_t kRowsStageTargetWide = 32 * 1024;     // wide shapes: at least two rows of 10 KB
 constexpr size_t kRowsBudget = 110 * 1024;             // two CTAs per SM: the next kernel starts early
 constexpr size_t kRowsBudgetWide = 200 * 1024;         // one CTA per SM
