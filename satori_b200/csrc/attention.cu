@@ -321,7 +321,8 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kStreamSlots;
     volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStreamSlots);
-    float (*P)[GMAX][kStreamTok] = reinterpret_cast<float (*)[GMAX][kStreamTok]>(smem + kStreamHeader);
+    // p of a warp's tile, token-major: the eight heads of token j are one 32-byte row.
+    float (*P)[kStreamTok][GMAX] = reinterpret_cast<float (*)[kStreamTok][GMAX]>(smem + kStreamHeader);
     uint8_t *slots = smem + kStreamHeader + kStreamPBytes;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -350,11 +351,13 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
     const int t1 = (int)(((long long)T * (split + 1)) / p.nsplit);
     const int nst = (t1 - t0 + kStreamTok - 1) / kStreamTok;
 
-    float acc[GMAX][DPL];
+    // acc[h][c] holds dims (2c, 2c+1) of this lane's 4 for head h: FP32x2 FMAs, each component rounded
+    // exactly as a scalar fmaf chain.
+    float2 acc[GMAX][DPL / 2];
 #pragma unroll
     for (int h = 0; h < GMAX; ++h)
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) acc[h][i] = 0.0f;
+        for (int c = 0; c < DPL / 2; ++c) acc[h][c] = make_float2(0.0f, 0.0f);
     float m_my = -INFINITY, l_my = 0.0f;
 
     if (warp == kStreamWarps) {
@@ -385,11 +388,14 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
                 mbar_wait_bounded(&full[j % kStreamSlots], (uint32_t)((j / kStreamSlots) & 1));
         }
     } else {
-        float qr[GMAX][DPL];
+        // q of head pairs (2g, 2g+1): one FP32x2 FMA advances both heads' dot products.
+        float2 qp[GMAX / 2][DPL];
 #pragma unroll
-        for (int h = 0; h < GMAX; ++h)
+        for (int g = 0; g < GMAX / 2; ++g)
 #pragma unroll
-            for (int i = 0; i < DPL; ++i) qr[h][i] = h < gc ? p.q[(h0 + h) * hd + 4 * lane + i] : 0.0f;
+            for (int i = 0; i < DPL; ++i)
+                qp[g][i] = make_float2(2 * g < gc ? p.q[(h0 + 2 * g) * hd + 4 * lane + i] : 0.0f,
+                                       2 * g + 1 < gc ? p.q[(h0 + 2 * g + 1) * hd + 4 * lane + i] : 0.0f);
         for (int k = warp; k < nst; k += kStreamWarps) {
             const int s = k % kStreamSlots;
             if (*abort_flag) break;
@@ -410,11 +416,12 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
                     const float kr[DPL] = {t4.x, t4.y, t4.z, t4.w};
                     float v[8];
 #pragma unroll
-                    for (int h = 0; h < 8; ++h) {
-                        float a = 0.0f;
+                    for (int g = 0; g < GMAX / 2; ++g) {
+                        float2 a = make_float2(0.0f, 0.0f);
 #pragma unroll
-                        for (int i = 0; i < DPL; ++i) a = fmaf(qr[h][i], kr[i], a);
-                        v[h] = a;
+                        for (int i = 0; i < DPL; ++i) a = __ffma2_rn(qp[g][i], make_float2(kr[i], kr[i]), a);
+                        v[2 * g] = a.x;
+                        v[2 * g + 1] = a.y;
                     }
                     sc[j] = transpose_reduce<GMAX>(v, lane) * p.scale;
                 } else {
@@ -431,26 +438,28 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
             for (int j = 0; j < kStreamTok; ++j) {
                 const float pj = j < nt ? expf(sc[j] - m_new) : 0.0f;
                 lsum += pj;
-                if ((j % R) == (lane % R)) P[warp][hl][j] = pj;
+                if ((j % R) == (lane % R)) P[warp][j][hl] = pj;
             }
             l_my = l_my * alpha + lsum;
             m_my = m_new;
-            float alpha_h[GMAX];
 #pragma unroll
-            for (int h = 0; h < GMAX; ++h) alpha_h[h] = __shfl_sync(0xFFFFFFFFu, alpha, h * R);
+            for (int h = 0; h < GMAX; ++h) {
+                const float ah = __shfl_sync(0xFFFFFFFFu, alpha, h * R);
 #pragma unroll
-            for (int h = 0; h < GMAX; ++h)
-#pragma unroll
-                for (int i = 0; i < DPL; ++i) acc[h][i] *= alpha_h[h];
+                for (int c = 0; c < DPL / 2; ++c) acc[h][c] = __fmul2_rn(acc[h][c], make_float2(ah, ah));
+            }
             __syncwarp();
             for (int j = 0; j < nt; ++j) {
                 const float4 t4 = lds128f(vt + 512u * j);
-                const float vr[DPL] = {t4.x, t4.y, t4.z, t4.w};
+                const float2 v01 = make_float2(t4.x, t4.y), v23 = make_float2(t4.z, t4.w);
+                const float4 pa = *reinterpret_cast<const float4 *>(&P[warp][j][0]);
+                const float4 pb = *reinterpret_cast<const float4 *>(&P[warp][j][4]);
+                const float pj[GMAX] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
                 for (int h = 0; h < GMAX; ++h) {
-                    const float pj = P[warp][h][j];
-#pragma unroll
-                    for (int i = 0; i < DPL; ++i) acc[h][i] = fmaf(pj, vr[i], acc[h][i]);
+                    const float2 pp = make_float2(pj[h], pj[h]);
+                    acc[h][0] = __ffma2_rn(pp, v01, acc[h][0]);
+                    acc[h][1] = __ffma2_rn(pp, v23, acc[h][1]);
                 }
             }
             __syncwarp();
@@ -468,9 +477,13 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
             wl[warp * GMAX + hl] = l_my;
         }
 #pragma unroll
-        for (int h = 0; h < GMAX; ++h)
-#pragma unroll
-            for (int i = 0; i < DPL; ++i) wacc[(warp * GMAX + h) * hd + 4 * lane + i] = acc[h][i];
+        for (int h = 0; h < GMAX; ++h) {
+            float *w = wacc + (warp * GMAX + h) * hd + 4 * lane;
+            w[0] = acc[h][0].x;
+            w[1] = acc[h][0].y;
+            w[2] = acc[h][1].x;
+            w[3] = acc[h][1].y;
+        }
     }
     __syncthreads();
     const int rec_stride = hd + 2;
