@@ -512,7 +512,7 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
 // latency-bound).  The arithmetic and its order are unchanged: max over splits, then l and each output
 // dim as sequential fmaf sums over the splits in split order.
 constexpr int kMergeThreads = 128;
-constexpr int kMergeChunk = 32;   // splits staged per round
+constexpr int kMergeChunk = 32;   // splits staged per round (small: the next kernel shares its SM)
 
 __device__ __forceinline__ void cp_async4(float *dst, const float *src)
 {
