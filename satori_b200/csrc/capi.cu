@@ -115,7 +115,7 @@ int upload_payload(satori_ctx *ctx, const uint8_t *src, bool src_is_device, size
 
 int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int format, int order, const float *dx,
              float *dy, int positions, int epilogue, const float *bias, float *residual, cudaStream_t stream,
-             int use_pdl, const float *norm_w, float norm_eps)
+             int use_pdl, const float *norm_w, float norm_eps, const XPush *xp, const XWait *xw)
 {
     const int per_launch = order == SATORI_ORDER_BATCH ? 8 : 1;
     for (int p0 = 0; p0 < positions; p0 += per_launch) {
@@ -138,13 +138,16 @@ int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int 
             a.use_pdl = use_pdl;
             a.norm_w = norm_w;
             a.norm_eps = norm_eps;
+            if (xp) a.xp = *xp;
+            if (xw) a.xw = *xw;
             DecodePlan dp = plan_gemv_rows(a, ctx->sm_count, ctx->smem_optin);
             if (dp.ok) {
                 cudaError_t e = launch_gemv_rows(a, dp, stream);
                 if (e != cudaSuccess) return cuda_fail(e, "launch decode MatVec");
                 continue;
             }
-            if (norm_w) return set_error(SATORI_ERR_NOT_SUPPORTED, "the fused RmsNorm needs the decode rows kernel");
+            if (norm_w || xp || xw)
+                return set_error(SATORI_ERR_NOT_SUPPORTED, "fused RmsNorm / peer exchange need the decode rows kernel");
             dp = plan_gemv_decode(a, ctx->sm_count, ctx->smem_optin);
             if (dp.ok) {
                 cudaError_t e = launch_gemv_decode(a, dp, stream);
@@ -152,8 +155,8 @@ int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int 
                 continue;
             }
         }
-        if (epilogue == kEpiSwiGlu || norm_w)
-            return set_error(SATORI_ERR_NOT_SUPPORTED, "fused SwiGLU / RmsNorm need the decode rows kernel");
+        if (epilogue == kEpiSwiGlu || norm_w || xp || xw)
+            return set_error(SATORI_ERR_NOT_SUPPORTED, "fused SwiGLU / RmsNorm / exchange need the decode rows kernel");
         GemvPlan plan = plan_gemv(rows, cols, format, np, ctx->sm_count, ctx->smem_optin);
         if (!plan.ok) return set_error(SATORI_ERR_ARGUMENT, "no MatVec plan fits shared memory for %dx%d", rows, cols);
         GemvArgs a = {};

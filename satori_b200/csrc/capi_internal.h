@@ -8,6 +8,7 @@
 #include <string>
 
 #include "../../include/satori_cuda.h"
+#include "xchg.cuh"
 
 struct satori_ctx {
     int device = 0;
@@ -48,6 +49,7 @@ int upload_payload(satori_ctx *ctx, const uint8_t *src, bool src_is_device, size
 // Runs the MatVec on device pointers with the library's plan for this shape.
 int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int format, int order,
              const float *dx, float *dy, int positions, int epilogue, const float *bias, float *residual,
-             cudaStream_t stream, int use_pdl, const float *norm_w = nullptr, float norm_eps = 0.0f);
+             cudaStream_t stream, int use_pdl, const float *norm_w = nullptr, float norm_eps = 0.0f,
+             const XPush *xp = nullptr, const XWait *xw = nullptr);
 
 }  // namespace satori

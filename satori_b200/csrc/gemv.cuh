@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "xchg.cuh"
+
 namespace satori {
 
 // Optional fused epilogue of the MatVec (decode-step glue; each reproduces the reference op):
@@ -29,6 +31,8 @@ struct GemvArgs {
     int use_pdl;             // launched with programmatic stream serialization
     const float *norm_w;     // non-null: x is RmsNorm'ed on the fly with these weights (gemv_rows only)
     float norm_eps;
+    XPush xp;                // sharded step: push the epilogue's output to the peers (gemv_rows only)
+    XWait xw;                // sharded step: wait for the peers' slices of x first (gemv_rows only)
 };
 
 // Geometry the host chooses for one launch.

@@ -64,6 +64,8 @@ struct RowsGeo {
     int use_pdl;
     const float *norm_w;  // non-null: RmsNorm x (TransformerOps.RmsNorm) before the products
     float norm_eps;
+    XPush xp;             // sharded step: the epilogue's output also goes to every peer (xchg.cuh)
+    XWait xw;             // sharded step: x holds peers' slices; wait for their signals before reading it
 };
 
 // Bounded wait until a shared counter reaches `target` (written by the control warp).
@@ -132,7 +134,7 @@ __device__ __forceinline__ bool rows_compute(const RowsGeo &g, uint8_t *smem, in
         wofs[k] = (uint32_t)(b * BB - PH);
         const float4 *xb = reinterpret_cast<const float4 *>(g.x) + (size_t)b * 8;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) xv[k][q] = xb[q];
+        for (int q = 0; q < 8; ++q) xv[k][q] = __ldcg(xb + q);   // L2: peers may have written x
         if (g.norm_w) {
             const float4 *wb = reinterpret_cast<const float4 *>(g.norm_w) + (size_t)b * 8;
 #pragma unroll
@@ -268,6 +270,11 @@ __global__ void __launch_bounds__(rows_threads(CW), CW == 8 ? 2 : 1) gemv_rows_k
         pdl_launch_dependents();
         pdl_wait();
     }
+    if (g.xw.world) {
+        // Sharded step: x holds slices the peers store; wait for all of them before anyone reads it.
+        if (tid == 0) xwait_peers(g.xw, g.err);
+        __syncthreads();
+    }
     if (g.norm_w) {
         // The RmsNorm scale of x: warps 0..7 form the fixed-order sum, every thread reads it back.
         if (tid < 256) rms_partial(g.x, g.bpr * 32, tid, h.red);
@@ -356,7 +363,11 @@ __global__ void __launch_bounds__(rows_threads(CW), CW == 8 ? 2 : 1) gemv_rows_k
             if (g.epilogue == kEpiSwiGlu) {
                 // Rows 2i and 2i + 1 are gate row i and up row i; batches and CTAs start on even rows.
                 const float up = __shfl_down_sync(nrows == 32 ? 0xFFFFFFFFu : (1u << nrows) - 1u, acc, 1);
-                if ((lane & 1) == 0) g.y[grow >> 1] = swiglu_value(acc, up);
+                if ((lane & 1) == 0) {
+                    const float a = swiglu_value(acc, up);
+                    g.y[grow >> 1] = a;
+                    if (g.xp.world) xpush_value(g.xp, grow >> 1, a);
+                }
             } else {
                 if (g.epilogue == kEpiBias) acc = fadd(acc, g.bias[grow]);
                 if (g.epilogue == kEpiResidual) {
@@ -364,10 +375,17 @@ __global__ void __launch_bounds__(rows_threads(CW), CW == 8 ? 2 : 1) gemv_rows_k
                     g.residual[grow] = acc;
                 }
                 g.y[grow] = acc;
+                // The gathered buffer is the residual stream for a residual epilogue, else y.
+                if (g.xp.world) xpush_value(g.xp, grow, acc);
             }
         }
         __syncwarp();
         if (lane == 0) *h.folded = fb + 1;
+    }
+    if (g.xp.world) {
+        __threadfence_system();   // this lane's peer stores, before the CTA counts as done
+        __syncwarp();
+        if (lane == 0) xpush_finish(g.xp);
     }
 }
 
@@ -504,6 +522,8 @@ cudaError_t launch_gemv_rows(const GemvArgs &a, const DecodePlan &plan, cudaStre
     g.use_pdl = a.use_pdl;
     g.norm_w = a.norm_w;
     g.norm_eps = a.norm_eps;
+    g.xp = a.xp;
+    g.xw = a.xw;
     const bool q8 = a.format == 0;
     if (plan.nb == 2) return q8 ? launch_rows<0, 12, 2>(g, plan, stream) : launch_rows<1, 12, 2>(g, plan, stream);
     switch (plan.cw) {

@@ -174,16 +174,39 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
     const int H = s->hidden, qw = s->q_width, hd = s->head_dim;
     const int group = s->q_heads / s->kv_heads;
     const int nq = s->qb - s->qa, nkv = s->kb - s->ka;
+    // Sharded P2P step: a row-MatVec launch that produces a gathered vector carries the exchange (its
+    // epilogue stores the rows into the peers' copies and signals), and the launch that reads the vector
+    // next waits for the peers' signals; `pending` tracks an exchange whose wait is still owed.
+    const bool xf = session_xchg_fusable(s);
+    const XWait xw = xf ? session_xwait(s) : XWait{};
+    bool pending = false;
+    auto take_wait = [&]() -> const XWait * {
+        if (!pending) return nullptr;
+        pending = false;
+        return &xw;
+    };
+    auto flush_wait = [&]() -> int {
+        if (!pending) return SATORI_OK;
+        pending = false;
+        return launch_xwait(s, st);
+    };
+    auto carries = [&](int rows, int cols, int fmt, int epi) {
+        return xf && gemv_rows_takes(rows, cols, fmt, epi, s->ctx->sm_count, s->ctx->smem_optin);
+    };
     TRYCUDA(launch_embed(s->embd.payload, H, s->d_token, s->d_pos, s->d_tokens, s->d_hidden, s->d_rope, s->rope_base,
                          hd, st, pdl),
             "embed");
     for (int l = 0; l < s->layers; ++l) {
         const Layer &L = s->layer[l];
-        if (!L.qkv_norm) TRYCUDA(launch_rmsnorm(s->d_hidden, L.attn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
+        if (!L.qkv_norm) {
+            TRY(flush_wait());
+            TRYCUDA(launch_rmsnorm(s->d_hidden, L.attn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
+        }
         if (L.qkv.payload) {
             TRY(run_gemv(s->ctx, L.qkv.payload, L.qkv.rows, H, L.qkv.format, SATORI_ORDER_BATCH,
                          L.qkv_norm ? s->d_hidden : s->d_normed, s->d_qkv, 1, L.qkv_bias ? kEpiBias : kEpiNone,
-                         L.qkv_bias, nullptr, st, pdl, L.qkv_norm ? L.attn_norm : nullptr, s->eps));
+                         L.qkv_bias, nullptr, st, pdl, L.qkv_norm ? L.attn_norm : nullptr, s->eps, nullptr,
+                         L.qkv_norm ? take_wait() : nullptr));
         } else {
             TRY(run_gemv(s->ctx, L.q.payload, L.q.rows, H, L.q.format, SATORI_ORDER_BATCH, s->d_normed, s->d_q, 1,
                          L.q_bias ? kEpiBias : kEpiNone, L.q_bias, nullptr, st, pdl));
@@ -241,31 +264,64 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
         } else {
             TRY(session_exchange(s, s->d_ctx, (size_t)s->qa * hd, (size_t)s->q_local, st));
         }
-        TRY(run_gemv(s->ctx, L.o.payload, s->h1 - s->h0, qw, L.o.format, SATORI_ORDER_BATCH, s->d_ctx,
-                     s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl));
-        TRY(session_exchange(s, s->d_hidden, (size_t)s->h0, (size_t)(s->h1 - s->h0), st));
+        if (carries(s->h1 - s->h0, qw, L.o.format, kEpiResidual)) {
+            const XPush xp = session_xpush(s, s->d_hidden + s->h0);
+            TRY(run_gemv(s->ctx, L.o.payload, s->h1 - s->h0, qw, L.o.format, SATORI_ORDER_BATCH, s->d_ctx,
+                         s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl, nullptr, 0.0f,
+                         &xp));
+            pending = true;
+        } else {
+            TRY(run_gemv(s->ctx, L.o.payload, s->h1 - s->h0, qw, L.o.format, SATORI_ORDER_BATCH, s->d_ctx,
+                         s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl));
+            TRY(session_exchange(s, s->d_hidden, (size_t)s->h0, (size_t)(s->h1 - s->h0), st));
+        }
         const int nf = s->f1 - s->f0;
         if (L.gu.payload) {
             // ffn_norm runs inside the launch: every CTA forms the same norm of the residual.
+            const XPush xp = xf ? session_xpush(s, s->d_act + s->f0) : XPush{};
             TRY(run_gemv(s->ctx, L.gu.payload, 2 * nf, H, L.gu.format, SATORI_ORDER_BATCH, s->d_hidden,
-                         s->d_act + s->f0, 1, kEpiSwiGlu, nullptr, nullptr, st, pdl, L.ffn_norm, s->eps));
+                         s->d_act + s->f0, 1, kEpiSwiGlu, nullptr, nullptr, st, pdl, L.ffn_norm, s->eps,
+                         xf ? &xp : nullptr, take_wait()));
+            if (xf)
+                pending = true;
+            else
+                TRY(session_exchange(s, s->d_act, (size_t)s->f0, (size_t)nf, st));
         } else {
+            TRY(flush_wait());
             TRYCUDA(launch_rmsnorm(s->d_hidden, L.ffn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
             TRY(run_gemv(s->ctx, L.gate.payload, nf, H, L.gate.format, SATORI_ORDER_BATCH, s->d_normed, s->d_gate, 1,
                          kEpiNone, nullptr, nullptr, st, pdl));
             TRY(run_gemv(s->ctx, L.up.payload, nf, H, L.up.format, SATORI_ORDER_BATCH, s->d_normed, s->d_up, 1,
                          kEpiNone, nullptr, nullptr, st, pdl));
             TRYCUDA(launch_swiglu(s->d_gate, s->d_up, nf, s->d_act + s->f0, st, pdl), "swiglu");
+            TRY(session_exchange(s, s->d_act, (size_t)s->f0, (size_t)nf, st));
         }
-        TRY(session_exchange(s, s->d_act, (size_t)s->f0, (size_t)nf, st));
-        TRY(run_gemv(s->ctx, L.down.payload, s->h1 - s->h0, s->ffn, L.down.format, SATORI_ORDER_BATCH, s->d_act,
-                     s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl));
-        TRY(session_exchange(s, s->d_hidden, (size_t)s->h0, (size_t)(s->h1 - s->h0), st));
+        if (carries(s->h1 - s->h0, s->ffn, L.down.format, kEpiResidual)) {
+            const XPush xp = session_xpush(s, s->d_hidden + s->h0);
+            TRY(run_gemv(s->ctx, L.down.payload, s->h1 - s->h0, s->ffn, L.down.format, SATORI_ORDER_BATCH,
+                         s->d_act, s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl,
+                         nullptr, 0.0f, &xp, take_wait()));
+            pending = true;
+        } else {
+            TRY(flush_wait());
+            TRY(run_gemv(s->ctx, L.down.payload, s->h1 - s->h0, s->ffn, L.down.format, SATORI_ORDER_BATCH,
+                         s->d_act, s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl));
+            TRY(session_exchange(s, s->d_hidden, (size_t)s->h0, (size_t)(s->h1 - s->h0), st));
+        }
     }
+    TRY(flush_wait());
     TRYCUDA(launch_rmsnorm(s->d_hidden, s->output_norm, H, s->eps, s->d_final, st, pdl), "final norm");
-    TRY(run_gemv(s->ctx, s->output.payload, s->v1 - s->v0, H, s->output.format, SATORI_ORDER_BATCH, s->d_final,
-                 s->d_logits + s->v0, 1, kEpiNone, nullptr, nullptr, st, pdl));
-    TRY(session_exchange(s, s->d_logits, (size_t)s->v0, (size_t)(s->v1 - s->v0), st));
+    if (carries(s->v1 - s->v0, H, s->output.format, kEpiNone)) {
+        const XPush xp = session_xpush(s, s->d_logits + s->v0);
+        TRY(run_gemv(s->ctx, s->output.payload, s->v1 - s->v0, H, s->output.format, SATORI_ORDER_BATCH, s->d_final,
+                     s->d_logits + s->v0, 1, kEpiNone, nullptr, nullptr, st, pdl, nullptr, 0.0f, &xp));
+        pending = true;
+    } else {
+        TRY(run_gemv(s->ctx, s->output.payload, s->v1 - s->v0, H, s->output.format, SATORI_ORDER_BATCH, s->d_final,
+                     s->d_logits + s->v0, 1, kEpiNone, nullptr, nullptr, st, pdl));
+        TRY(session_exchange(s, s->d_logits, (size_t)s->v0, (size_t)(s->v1 - s->v0), st));
+    }
+    TRY(flush_wait());
     TRYCUDA(launch_argmax_advance(s->d_logits, s->vocab, s->d_argmax, s->d_nonfinite, s->d_pos, s->d_token,
                                   reinterpret_cast<unsigned *>(s->d_ints + 8), s->ctx->sm_count, st, pdl),
             "argmax");

@@ -100,6 +100,14 @@ bool session_p2p(const satori_session *s);
 int session_exchange_alloc(satori_session *s);
 // Gathers buf[off, off + count) from every rank (each rank its own slice) into every rank's buf.
 int session_exchange(satori_session *s, float *buf, size_t off, size_t count, cudaStream_t st);
+// P2P backend: a producing row-MatVec launch can carry the exchange itself (xchg.cuh).  session_xpush
+// describes the push of an output whose element 0 is `local_out` (inside the exchange arena);
+// session_xwait the wait of its consumer; launch_xwait runs that wait alone, for a consumer that
+// cannot carry it.
+bool session_xchg_fusable(const satori_session *s);
+satori::XPush session_xpush(satori_session *s, float *local_out);
+satori::XWait session_xwait(satori_session *s);
+int launch_xwait(satori_session *s, cudaStream_t st);
 // Copies every rank's query-head block out of the padded exchange buffer into d_ctx.
 cudaError_t launch_ctx_compact(const float *pad, float *ctx, int world, int q_heads, int head_dim, int qmax,
                                cudaStream_t st);

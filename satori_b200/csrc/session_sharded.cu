@@ -35,6 +35,7 @@
 #include "capi_internal.h"
 #include "common.cuh"
 #include "session_internal.h"
+#include "xchg.cuh"
 
 using namespace satori;
 
@@ -84,7 +85,7 @@ __global__ void ctx_compact_kernel(const float *pad, float *ctx, int world, int 
     }
 }
 
-constexpr int kMaxRanks = 8;
+constexpr int kMaxRanks = kXchgMaxRanks;
 constexpr int kPushThreads = 256;
 constexpr int kPushMaxCtas = 16;
 // Default wait for a peer's signal: about four seconds of SM clock at 1.965 GHz, far above any step, so
@@ -110,18 +111,6 @@ struct PushArgs {
     long long budget;                      // SM cycles to wait for the peers' signals
     int rank, world;
 };
-
-__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v)
-{
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p)
-{
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
 
 // One exchange: copy this rank's slice to every peer, then signal and wait (last CTA to finish).
 __global__ void __launch_bounds__(kPushThreads) p2p_push_kernel(PushArgs a)
@@ -151,11 +140,11 @@ __global__ void __launch_bounds__(kPushThreads) p2p_push_kernel(PushArgs a)
     const unsigned long long n = a.own->seq + 1;
     __threadfence_system();
     for (int p = 0; p < a.world; ++p)
-        if (p != a.rank) st_release_sys(a.signal[p], n);
+        if (p != a.rank) xchg_store_release_sys(a.signal[p], n);
     const long long start = clock64();
     for (int p = 0; p < a.world; ++p) {
         if (p == a.rank) continue;
-        while (ld_acquire_sys(&a.own->flag[p]) < n) {
+        while (xchg_load_acquire_sys(&a.own->flag[p]) < n) {
             // After one expired wait the rest of the step does not wait again: the step already failed.
             if (clock64() - start > a.budget || (*(volatile unsigned *)a.err & kDevErrTimeout)) {
                 atomicOr(a.err, kDevErrTimeout);
@@ -168,6 +157,14 @@ __global__ void __launch_bounds__(kPushThreads) p2p_push_kernel(PushArgs a)
     a.own->seq = n;
 }
 
+// The wait of an exchange carried by its producer, for a consumer that cannot carry it.
+__global__ void xwait_kernel(XWait w, unsigned *err)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    if (threadIdx.x == 0) xwait_peers(w, err);
+}
+
 }  // namespace
 
 struct ShardState {
@@ -177,6 +174,7 @@ struct ShardState {
     char *peer[kMaxRanks] = {};            // every rank's arena as mapped here (peer[rank] == arena)
     size_t arena_bytes = 0;
     long long wait_cycles = kPeerWaitCycles;
+    bool carry = false;                    // producing MatVec launches carry their exchanges (opt-in)
 };
 
 int session_plan_shards(satori_session *s)
@@ -273,6 +271,56 @@ int session_exchange_alloc(satori_session *s)
                              s->rank, p, cudaGetErrorString(e));
         sh->peer[p] = static_cast<char *>(m);
     }
+    return SATORI_OK;
+}
+
+bool session_xchg_fusable(const satori_session *s)
+{
+    return s->world > 1 && s->shard && s->shard->p2p && s->shard->carry;
+}
+
+XPush session_xpush(satori_session *s, float *local_out)
+{
+    ShardState *sh = s->shard;
+    XPush x = {};
+    const size_t at = (size_t)(reinterpret_cast<char *>(local_out) - sh->arena);
+    for (int p = 0; p < s->world; ++p) {
+        if (p == s->rank) continue;
+        x.dst[p] = reinterpret_cast<float *>(sh->peer[p] + at);
+        x.signal[p] = &reinterpret_cast<ArenaHeader *>(sh->peer[p])->flag[s->rank];
+    }
+    ArenaHeader *own = reinterpret_cast<ArenaHeader *>(sh->arena);
+    x.ticket = &own->ticket;
+    x.seq = &own->seq;
+    x.world = s->world;
+    x.rank = s->rank;
+    return x;
+}
+
+XWait session_xwait(satori_session *s)
+{
+    ArenaHeader *own = reinterpret_cast<ArenaHeader *>(s->shard->arena);
+    XWait w = {};
+    w.flags = own->flag;
+    w.seq = &own->seq;
+    w.budget = s->shard->wait_cycles;
+    w.world = s->world;
+    w.rank = s->rank;
+    return w;
+}
+
+int launch_xwait(satori_session *s, cudaStream_t st)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = s->use_pdl ? 1 : 0;
+    TRYCUDA(cudaLaunchKernelEx(&cfg, xwait_kernel, session_xwait(s), s->ctx->d_err), "exchange wait");
     return SATORI_OK;
 }
 
@@ -389,6 +437,7 @@ extern "C" int satori_session_create_sharded(satori_ctx *ctx, const satori_model
     s->shard = new ShardState();
     s->shard->comm = comm;
     s->shard->p2p = p2p;
+    if (const char *c = getenv("SATORI_EXCHANGE_CARRY")) s->shard->carry = strcmp(c, "1") == 0;
     if (const char *ms = getenv("SATORI_PEER_TIMEOUT_MS")) {
         const long long v = atoll(ms);
         if (v > 0) s->shard->wait_cycles = v * 2000000LL;   // 2 GHz: at most the B200's SM clock

@@ -4,7 +4,9 @@ Projections are sharded by rows, so every logit is produced by the same per-row 
 one GPU; attention is sharded by query heads.  Every rank must hold the same full logits (bitwise:
 they are all-gathered), within the single-GPU tolerance of the oracle, with identical greedy tokens.
 The shapes cover an even head split, a split that cuts a GQA group (two ranks compute one KV head),
-and an uneven query-head split (padded context exchange).
+and an uneven query-head split (padded context exchange).  Backends: P2P with one exchange kernel per
+all-gather, P2P with the exchanges carried by the producing row-MatVec launches where the shape allows
+(hidden 256 takes that path for every projection), and NCCL.
 """
 import multiprocessing as mp
 import os
@@ -64,7 +66,8 @@ def _run_world(sat, world, spec_kwargs, seed, context, tokens, gen_first, gen_co
     codes = _spawn(shard_worker.run_rank,
                    [(r, world, nccl_id, spec_kwargs, seed, context, tokens, gen_first, gen_count, outs[r])
                     for r in range(world)],
-                   {"NCCL_NVLS_ENABLE": "0", "SATORI_EXCHANGE": backend})
+                   {"NCCL_NVLS_ENABLE": "0", "SATORI_EXCHANGE": backend.split("-")[0],
+                    "SATORI_EXCHANGE_CARRY": "1" if backend.endswith("-carry") else "0"})
     assert codes == [0] * world
     return [np.load(o) for o in outs]
 
@@ -78,7 +81,7 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("backend", ["p2p", "nccl"])
+@pytest.mark.parametrize("backend", ["p2p", "p2p-carry", "nccl"])
 @pytest.mark.parametrize("world,kw", CASES)
 def test_sharded_session_matches_oracle(sat, oracle_lib, tmp_path, world, kw, backend):
     if _gpu_count() < world:
