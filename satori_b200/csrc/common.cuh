@@ -51,10 +51,7 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t bits16)
 __device__ __forceinline__ void rms_partial(const float *x, int n, int tid, double *red)
 {
     double sum = 0;
-    for (int i = tid; i < n; i += 256) {
-        const double v = __ldcg(x + i);   // L2: in a sharded step peers write parts of x
-        sum = __dadd_rn(sum, __dmul_rn(v, v));
-    }
+    for (int i = tid; i < n; i += 256) sum = __dadd_rn(sum, __dmul_rn((double)x[i], (double)x[i]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum = __dadd_rn(sum, __shfl_xor_sync(0xFFFFFFFFu, sum, o));
     if ((tid & 31) == 0) red[tid >> 5] = sum;

@@ -134,7 +134,7 @@ __device__ __forceinline__ bool rows_compute(const RowsGeo &g, uint8_t *smem, in
         wofs[k] = (uint32_t)(b * BB - PH);
         const float4 *xb = reinterpret_cast<const float4 *>(g.x) + (size_t)b * 8;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) xv[k][q] = __ldcg(xb + q);   // L2: peers may have written x
+        for (int q = 0; q < 8; ++q) xv[k][q] = xb[q];
         if (g.norm_w) {
             const float4 *wb = reinterpret_cast<const float4 *>(g.norm_w) + (size_t)b * 8;
 #pragma unroll
@@ -271,7 +271,8 @@ __global__ void __launch_bounds__(rows_threads(CW), CW == 8 ? 2 : 1) gemv_rows_k
         pdl_wait();
     }
     if (g.xw.world) {
-        // Sharded step: x holds slices the peers store; wait for all of them before anyone reads it.
+        // Sharded step: x holds slices the peers store; wait for all of them before anyone reads it (the
+        // acquire load of the peers' flags, then the barrier, orders every thread's later loads of x).
         if (tid == 0) xwait_peers(g.xw, g.err);
         __syncthreads();
     }

@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const floa
     rms_partial(x, n, threadIdx.x, red);
     __syncthreads();
     const double scale = rms_scale(red, n, eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = rms_apply(__ldcg(x + i), scale, w[i]);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = rms_apply(x[i], scale, w[i]);
 }
 
 __global__ void rmsnorm_heads_kernel(float *v, int n, const float *w, float eps, int hd, int pdl)
@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float *log
     unsigned long long best = 0;
     bool bad = false;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const float v = __ldcg(logits + i);   // L2: in a sharded step peers write most of the logits
+        const float v = logits[i];
         bad |= !isfinite(v);
         const unsigned long long k = argmax_key(v, i);
         best = k > best ? k : best;
