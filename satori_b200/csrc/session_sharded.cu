@@ -174,7 +174,7 @@ struct ShardState {
     char *peer[kMaxRanks] = {};            // every rank's arena as mapped here (peer[rank] == arena)
     size_t arena_bytes = 0;
     long long wait_cycles = kPeerWaitCycles;
-    bool carry = false;                    // producing MatVec launches carry their exchanges (opt-in)
+    bool carry = true;                     // producing MatVec launches carry their exchanges
 };
 
 int session_plan_shards(satori_session *s)
@@ -437,7 +437,7 @@ extern "C" int satori_session_create_sharded(satori_ctx *ctx, const satori_model
     s->shard = new ShardState();
     s->shard->comm = comm;
     s->shard->p2p = p2p;
-    if (const char *c = getenv("SATORI_EXCHANGE_CARRY")) s->shard->carry = strcmp(c, "1") == 0;
+    if (const char *c = getenv("SATORI_EXCHANGE_CARRY")) s->shard->carry = strcmp(c, "0") != 0;
     if (const char *ms = getenv("SATORI_PEER_TIMEOUT_MS")) {
         const long long v = atoll(ms);
         if (v > 0) s->shard->wait_cycles = v * 2000000LL;   // 2 GHz: at most the B200's SM clock

@@ -81,7 +81,7 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("backend", ["p2p", "p2p-carry", "nccl"])
+@pytest.mark.parametrize("backend", ["p2p-carry", "p2p-kernel", "nccl"])
 @pytest.mark.parametrize("world,kw", CASES)
 def test_sharded_session_matches_oracle(sat, oracle_lib, tmp_path, world, kw, backend):
     if _gpu_count() < world:
