@@ -10,10 +10,13 @@
 //
 // Two exchange backends:
 //  * P2P (default): the four gathered vectors live in one device arena per rank that every peer maps
-//    (CUDA IPC).  One small kernel per exchange stores this rank's slice into every peer's copy over
-//    NVLink, then signals each peer with a release store of the exchange's sequence number and waits
-//    (bounded) until every peer has signalled it.  Slices may differ in length, so an uneven query-head
-//    split needs no padding.
+//    (CUDA IPC).  Where the vector comes out of a row-MatVec launch, that launch stores its rows into
+//    every peer's copy as it writes them and signals from its last CTA, and the next launch waits
+//    (xchg.cuh); otherwise one small kernel per exchange stores this rank's slice into every peer's
+//    copy over NVLink, then signals each peer with a release store of the exchange's sequence number
+//    and waits (bounded) until every peer has signalled it (SATORI_EXCHANGE_CARRY=0 uses the kernel
+//    for every exchange).  Slices may differ in length, so an uneven query-head split needs no
+//    padding.
 //  * NCCL (SATORI_EXCHANGE=nccl): in-place ncclAllGather; an uneven query-head split goes through a
 //    padded context buffer and a compaction kernel.
 // NCCL also carries the IPC handles at creation.  It is loaded at run time (dlopen of libnccl.so.2),
