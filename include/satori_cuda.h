@@ -139,7 +139,10 @@ SATORI_API int satori_grouped_attention(satori_ctx *ctx, const float *q, const f
  * cudaStream_t (NULL = legacy default stream) on the current device.  The call allocates nothing; its
  * first call on a device looks up that array's address, so make that first call before any stream
  * capture.  Shapes whose partial records exceed 1,048,576 floats are rejected with
- * SATORI_ERR_ARGUMENT.  Calls share the one array: two calls that overlap on the GPU race. */
+ * SATORI_ERR_ARGUMENT.  Calls share the one array: two calls that overlap on the GPU race.  The call
+ * returns before the GPU runs, so unlike the context entry point it reports no SATORI_ERR_TIMEOUT: a
+ * bounded wait that expires inside the streaming kernel instead sends the affected heads to the FP64
+ * recomputation from K and V. */
 SATORI_API int satori_grouped_attention_noalloc(const float *q, const float *keys, const float *values,
                                                 int q_heads, int kv_heads, int head_dim, int tokens, float *out,
                                                 void *stream);
@@ -185,8 +188,9 @@ SATORI_API int satori_session_create(satori_ctx *ctx, const satori_model_desc *d
  * of `world`, one process per GPU, all ranks calling together.  Every projection is row-sharded (a
  * row's FP32 chain stays on one GPU, so logits equal the single-GPU session's); attention is sharded
  * by query heads, each rank caching only the KV heads its heads read; the context, the residual
- * after attn_output / ffn_down, the SwiGLU activations and the logits are all-gathered with NCCL
- * inside the step's CUDA graph.  hidden, ffn and vocab must be multiples of `world`
+ * after attn_output / ffn_down, the SwiGLU activations and the logits are all-gathered inside the
+ * step's CUDA graph -- by default with peer stores over NVLink into IPC-mapped buffers, carried by the
+ * producing MatVec launches where they can (SATORI_EXCHANGE=nccl selects NCCL all-gathers).  hidden, ffn and vocab must be multiples of `world`
  * (SATORI_ERR_NOT_SUPPORTED otherwise).  Every rank passes the full tensor table and uploads only
  * its rows.  `nccl_unique_id` is the 128-byte id from satori_nccl_unique_id on rank 0.  world = 1 is
  * satori_session_create. */
@@ -206,6 +210,15 @@ SATORI_API int satori_session_append_tokens(satori_session *s, const int *tokens
 SATORI_API int satori_session_generate(satori_session *s, int first, int count, int *tokens_out);
 SATORI_API int satori_session_position(const satori_session *s, int *position);
 SATORI_API int satori_session_reset(satori_session *s);    /* DenseSession.Reset (:189) */
+/* No counterpart in the reference (its DenseSession only resets to position 0): discards the
+ * positions at and after `position` (0 <= position <= the current position), keeping the cached
+ * K/V of the earlier ones, so a prompt's cache can be decoded from again without re-running it. */
+SATORI_API int satori_session_rewind(satori_session *s, int position);
+/* No counterpart in the reference: kernels launched per decode step (the captured graph's kernel
+ * nodes), payload bytes of the weights this session (or rank) holds, and the bytes of K/V one cached
+ * position occupies on this device (every decode step reads that much per position of context). */
+SATORI_API int satori_session_info(const satori_session *s, int *kernels_per_step, size_t *weight_bytes,
+                                   size_t *kv_bytes_per_position);
 /* Copies a stage tensor of the last step to the host: 0 = hidden after the last layer,
  * 1 = final_norm output, 2 = logits (stage parity, ForwardObserver in DenseForward.cs:6). */
 SATORI_API int satori_session_stage(const satori_session *s, int which, float *out, size_t n);

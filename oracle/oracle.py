@@ -44,6 +44,7 @@ def lib() -> C.CDLL:
         L.so_session_create.argtypes = [C.c_void_p, C.c_int]
         L.so_session_destroy.argtypes = [C.c_void_p]
         L.so_session_reset.argtypes = [C.c_void_p]
+        L.so_session_fill_cache.argtypes = [C.c_void_p, C.c_int, C.c_uint32]
         L.so_session_position.argtypes = [C.c_void_p]
         L.so_session_append.argtypes = [C.c_void_p, C.c_int, _f32p, _i32p, C.c_int]
         L.so_session_stage.argtypes = [C.c_void_p, C.c_int, _f32p, C.c_int]
@@ -329,6 +330,10 @@ class OracleSession:
 
     def reset(self):
         lib().so_session_reset(self._s)
+
+    def fill_cache(self, position: int, seed: int = 1):
+        """Benchmark helper: seeded cache rows [0, position) and position = `position`."""
+        _check(lib().so_session_fill_cache(self._s, int(position), int(seed)), "session_fill_cache")
 
     def close(self):
         if self._s:

@@ -772,6 +772,28 @@ void so_session_destroy(so_session *s)
 }
 
 void so_session_reset(so_session *s) { s->position = 0; }
+
+/* Benchmark helper (no reference counterpart): fills cache rows [0, position) of every layer with
+ * seeded values in [-1, 1) (Xorshift32) and moves the session to `position`, so a decode step at a
+ * long context can be timed without running the prompt first.  Decode cost depends only on the
+ * context length, not on the cached values. */
+int so_session_fill_cache(so_session *s, int position, uint32_t seed)
+{
+    if (position < 0 || position > s->context) return SO_ERR_ARGUMENT;
+    uint32_t x = seed ? seed : 1u;
+    for (int l = 0; l < s->m->layers; l++) {
+        float *k = s->keys + (size_t)l * s->context * s->kv_width;
+        float *v = s->values + (size_t)l * s->context * s->kv_width;
+        for (size_t i = 0; i < (size_t)position * s->kv_width; i++) {
+            x ^= x << 13; x ^= x >> 17; x ^= x << 5;
+            k[i] = (float)(x >> 8) * (1.0f / 8388608.0f) - 1.0f;
+            x ^= x << 13; x ^= x >> 17; x ^= x << 5;
+            v[i] = (float)(x >> 8) * (1.0f / 8388608.0f) - 1.0f;
+        }
+    }
+    s->position = position;
+    return SO_OK;
+}
 int so_session_position(const so_session *s) { return s->position; }
 
 /* DenseForward.Step (DenseForward.cs:100-162) for one layer at s->position. */

@@ -102,6 +102,7 @@ typedef struct so_session so_session;
 so_session *so_session_create(const so_model *model, int context);
 void so_session_destroy(so_session *s);
 void so_session_reset(so_session *s);
+int so_session_fill_cache(so_session *s, int position, uint32_t seed);
 int so_session_position(const so_session *s);
 /* Appends one token; writes logits [vocab] and the greedy token.  threads parallelises rows/heads only. */
 int so_session_append(so_session *s, int token, float *logits, int *argmax, int threads);

@@ -119,6 +119,8 @@ _SIGS = {
     "satori_session_generate": (C.c_int, [_vp, C.c_int, C.c_int, _vp]),
     "satori_session_position": (C.c_int, [_vp, _i32p]),
     "satori_session_reset": (C.c_int, [_vp]),
+    "satori_session_rewind": (C.c_int, [_vp, C.c_int]),
+    "satori_session_info": (C.c_int, [_vp, _i32p, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
     "satori_session_stage": (C.c_int, [_vp, C.c_int, _vp, C.c_size_t]),
     "satori_session_destroy": (C.c_int, [_vp]),
 }

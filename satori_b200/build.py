@@ -26,7 +26,6 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC,-O2,-fvisibility=hidden",
     "-Xptxas", "-O3",
     "--expt-relaxed-constexpr",
-    "-shared",
 ]
 
 
@@ -53,13 +52,29 @@ def stale() -> bool:
     return any(os.path.getmtime(p) > built for p in _inputs())
 
 
+def _compile(src: str, extra, verbose: bool) -> str:
+    obj = os.path.join(BUILD_DIR, os.path.basename(src)[:-3] + ".o")
+    cmd = [_nvcc(), *NVCC_FLAGS, *extra, "-c", "-o", obj, src]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    return obj
+
+
 def build(force: bool = False, verbose: bool = False, extra=()) -> str:
-    """Compile the library when it is missing or older than its sources; return its path."""
+    """Compile the library when it is missing or older than its sources; return its path.
+
+    Every ``.cu`` is compiled to its own object in parallel (each is a whole-program device unit: no
+    device code crosses files), then nvcc links them into the shared library."""
     if not (force or stale()):
         return LIB_PATH
+    from concurrent.futures import ThreadPoolExecutor
     os.makedirs(BUILD_DIR, exist_ok=True)
+    srcs = sources()
+    with ThreadPoolExecutor(max_workers=max(1, min(len(srcs), os.cpu_count() or 1))) as pool:
+        objs = list(pool.map(lambda s: _compile(s, extra, verbose), srcs))
     tmp = LIB_PATH + ".tmp"
-    cmd = [_nvcc(), *NVCC_FLAGS, *extra, "-o", tmp, *sources(), "-lcuda", "-ldl"]
+    cmd = [_nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs, "-lcuda", "-ldl"]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

@@ -487,6 +487,10 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
     }
     __syncthreads();
     const int rec_stride = hd + 2;
+    // A wait that ran out left tiles unread: the split's records become NaN, which sends every head the
+    // split serves to the merge kernel's FP64 recomputation from K and V instead of a silently partial
+    // sum (this also covers callers that pass no error word).
+    const bool aborted = *abort_flag != 0;
     for (int idx = tid; idx < gc * rec_stride; idx += blockDim.x) {
         const int h = idx / rec_stride, e = idx - h * rec_stride;
         float m = wm[h];
@@ -503,7 +507,7 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
                 val = fmaf(x, f, val);
             }
         }
-        p.scratch[((long long)split * p.q_heads + h0 + h) * rec_stride + e] = val;
+        p.scratch[((long long)split * p.q_heads + h0 + h) * rec_stride + e] = aborted ? __int_as_float(0x7fc00000) : val;
     }
 }
 
@@ -745,15 +749,10 @@ bool launch_stream(const AttnArgs &a, AttnParams &p, int gmax, int sm_count, cud
         return false;
     // About one CTA per SM (each keeps ~64 KB in flight); never more splits than the scratch holds.
     p.nsplit = std::max(1, std::min(p.nsplit, (sm_count + units - 1) / units));
-    static bool configured = false;
-    if (!configured) {
-        const cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   (int)kStreamSmem);
-        if (e != cudaSuccess) {
-            *err = e;
-            return true;
-        }
-        configured = true;
+    const cudaError_t e = opt_in_smem(reinterpret_cast<const void *>(attn_stream_kernel), kStreamSmem);
+    if (e != cudaSuccess) {
+        *err = e;
+        return true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.nsplit, units);
@@ -803,11 +802,8 @@ cudaError_t launch_attention(const AttnArgs &a, int sm_count, cudaStream_t strea
     cfg.gridDim = dim3(a.q_heads);
     cfg.blockDim = dim3(kMergeThreads);
     cfg.dynamicSmemBytes = sizeof(float) * ((size_t)((p.nsplit + 3) & ~3) + (size_t)kMergeChunk * (a.head_dim + 2));
-    if (cfg.dynamicSmemBytes > 48 * 1024) {
-        const cudaError_t ea = cudaFuncSetAttribute(attn_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                    (int)cfg.dynamicSmemBytes);
-        if (ea != cudaSuccess) return ea;
-    }
+    const cudaError_t ea = opt_in_smem(reinterpret_cast<const void *>(attn_merge_kernel), cfg.dynamicSmemBytes);
+    if (ea != cudaSuccess) return ea;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -13,6 +13,9 @@
 #include <string.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <utility>
 #include <vector>
 
 #define SATORI_VERSION "0.1.0"
@@ -40,6 +43,22 @@ int cuda_fail(cudaError_t e, const char *what)
     if (e == cudaErrorMemoryAllocation)
         return set_error(SATORI_ERR_OUT_OF_MEMORY, "%s: %s", what, cudaGetErrorString(e));
     return set_error(SATORI_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+cudaError_t opt_in_smem(const void *kernel, size_t bytes)
+{
+    if (bytes <= 48 * 1024) return cudaSuccess;   // the default limit needs no opt-in
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    static std::mutex lock;
+    static std::map<std::pair<const void *, int>, size_t> granted;
+    std::lock_guard<std::mutex> guard(lock);
+    size_t &have = granted[std::make_pair(kernel, dev)];
+    if (have >= bytes) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) have = bytes;
+    return e;
 }
 
 cudaError_t clear_dev_error(satori_ctx *ctx) { return cudaMemsetAsync(ctx->d_err, 0, sizeof(unsigned), ctx->stream); }

@@ -19,6 +19,12 @@ enum : unsigned { kDevErrTimeout = 1u };
 // Spin budget for mbarrier waits: ~4e9 cycles of polling is seconds, far beyond any copy.
 constexpr long long kWaitBudgetCycles = 4000000000LL;
 
+// --------------------------------------------------------------------------- launch set-up (host)
+// Opts `kernel` in to `bytes` of dynamic shared memory on the CURRENT device.  The attribute belongs to
+// a device's context, so the opt-in is remembered per (kernel, device) -- a process that launches on
+// several GPUs sets it on each -- under a lock, so concurrent callers on different threads are safe.
+cudaError_t opt_in_smem(const void *kernel, size_t bytes);
+
 // --------------------------------------------------------------------------- exact FP32 ops
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }

@@ -435,12 +435,8 @@ cudaError_t launch_one(const Geo &g, const GemvPlan &plan, cudaStream_t stream)
 {
     auto kern = gemv_kernel<FMT, ORDER, PMAX>;
     // Opt in to exactly the dynamic shared memory this plan needs (the limit counts static smem too).
-    static size_t configured = 48 * 1024;
-    if (plan.smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
-        if (e != cudaSuccess) return e;
-        configured = plan.smem;
-    }
+    const cudaError_t e = opt_in_smem(reinterpret_cast<const void *>(kern), plan.smem);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(plan.grid);
     cfg.blockDim = dim3(kThreads);

@@ -337,12 +337,8 @@ template <int FMT>
 cudaError_t launch_decode(const CUtensorMap &map, const DecGeo &g, const DecodePlan &plan, cudaStream_t stream)
 {
     auto kern = gemv_decode_kernel<FMT>;
-    static size_t configured = 48 * 1024;
-    if (plan.smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
-        if (e != cudaSuccess) return e;
-        configured = plan.smem;
-    }
+    const cudaError_t e = opt_in_smem(reinterpret_cast<const void *>(kern), plan.smem);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(plan.grid);
     cfg.blockDim = dim3(kDecThreads);

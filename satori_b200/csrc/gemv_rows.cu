@@ -394,12 +394,8 @@ template <int FMT, int CW, int NB>
 cudaError_t launch_rows(const RowsGeo &g, const DecodePlan &plan, cudaStream_t stream)
 {
     auto kern = gemv_rows_kernel<FMT, CW, NB>;
-    static size_t configured = 48 * 1024;
-    if (plan.smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
-        if (e != cudaSuccess) return e;
-        configured = plan.smem;
-    }
+    const cudaError_t e = opt_in_smem(reinterpret_cast<const void *>(kern), plan.smem);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(plan.grid);
     cfg.blockDim = dim3(rows_threads(CW));

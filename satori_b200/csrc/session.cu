@@ -340,6 +340,21 @@ static int build_graph(satori_session *s)
         return rc;
     }
     if (e != cudaSuccess) return cuda_fail(e, "end capture");
+    size_t nodes = 0;
+    e = cudaGraphGetNodes(g, nullptr, &nodes);
+    if (e == cudaSuccess && nodes) {
+        std::vector<cudaGraphNode_t> list(nodes);
+        e = cudaGraphGetNodes(g, list.data(), &nodes);
+        s->kernels_per_step = 0;
+        for (size_t i = 0; e == cudaSuccess && i < nodes; ++i) {
+            cudaGraphNodeType t;
+            if (cudaGraphNodeGetType(list[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++s->kernels_per_step;
+        }
+    }
+    if (e != cudaSuccess) {
+        cudaGraphDestroy(g);
+        return cuda_fail(e, "graph nodes");
+    }
     e = cudaGraphInstantiate(&s->graph_exec, g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) return cuda_fail(e, "instantiate graph");
@@ -425,6 +440,7 @@ int session_alloc_state(satori_session *s)
     TRY(dalloc(s, &s->d_gate, s->f1 - s->f0));
     TRY(dalloc(s, &s->d_up, s->f1 - s->f0));
     TRY(dalloc(s, &s->d_ints, 12));   // 0-6 step state (read back), 8-11 argmax scratch
+    TRY(dalloc(s, &s->d_gen, (size_t)s->context));
     TRY(dalloc(s, &s->d_rope, (size_t)s->head_dim));
     s->d_token = s->d_ints + 0;
     s->d_pos = s->d_ints + 1;
@@ -576,8 +592,7 @@ extern "C" int satori_session_generate(satori_session *s, int first, int count, 
         return set_error(SATORI_ERR_CONTEXT_FULL, "Context limit %d reached; reset or enlarge the session.", s->context);
     cudaStream_t st = s->ctx->stream;
     std::vector<int> out(count);
-    int *d_out = nullptr;
-    TRYCUDA(cudaMalloc(&d_out, sizeof(int) * count), "alloc tokens");
+    int *d_out = s->d_gen;            // count <= context - position <= context
     s->h_ints[7] = first;
     cudaError_t e = cudaMemcpyAsync(s->d_token, &s->h_ints[7], sizeof(int), cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = clear_dev_error(s->ctx);
@@ -589,7 +604,6 @@ extern "C" int satori_session_generate(satori_session *s, int first, int count, 
     if (e == cudaSuccess) e = cudaMemcpyAsync(out.data(), d_out, sizeof(int) * count, cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(s->h_ints, s->d_ints, 7 * sizeof(int), cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-    cudaFree(d_out);
     if (e != cudaSuccess) return cuda_fail(e, "generate");
     int rc = step_status(s);
     s->position += count;
@@ -616,6 +630,30 @@ extern "C" int satori_session_reset(satori_session *s)
     cudaError_t e = cudaMemsetAsync(s->d_pos, 0, sizeof(int), s->ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s->ctx->stream);
     return e == cudaSuccess ? SATORI_OK : cuda_fail(e, "reset");
+}
+
+extern "C" int satori_session_rewind(satori_session *s, int position)
+{
+    if (!s) return set_error(SATORI_ERR_DISPOSED, "session is disposed");
+    if (position < 0 || position > s->position)
+        return set_error(SATORI_ERR_ARGUMENT, "position %d is outside the committed range [0, %d]", position,
+                         s->position);
+    // The cache rows below `position` are untouched; the next step overwrites row `position`.
+    s->position = position;
+    s->h_ints[6] = position;
+    cudaError_t e = cudaMemcpyAsync(s->d_pos, &s->h_ints[6], sizeof(int), cudaMemcpyHostToDevice, s->ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->ctx->stream);
+    return e == cudaSuccess ? SATORI_OK : cuda_fail(e, "rewind");
+}
+
+extern "C" int satori_session_info(const satori_session *s, int *kernels_per_step, size_t *weight_bytes,
+                                   size_t *kv_bytes_per_position)
+{
+    if (!s) return set_error(SATORI_ERR_DISPOSED, "session is disposed");
+    if (kernels_per_step) *kernels_per_step = s->kernels_per_step;
+    if (weight_bytes) *weight_bytes = s->weight_bytes;
+    if (kv_bytes_per_position) *kv_bytes_per_position = (size_t)s->layers * 2 * s->kv_local * sizeof(float);
+    return SATORI_OK;
 }
 
 extern "C" int satori_session_stage(const satori_session *s, int which, float *out, size_t n)

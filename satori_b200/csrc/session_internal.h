@@ -67,6 +67,8 @@ struct satori_session {
     float *h_logits = nullptr;
 
     cudaGraphExec_t graph_exec = nullptr;
+    int kernels_per_step = 0;        // kernel nodes of the captured step
+    int *d_gen = nullptr;            // generated tokens of satori_session_generate ([context])
     std::vector<void *> allocations;
 
     // This rank's share of every dimension (a single-GPU session is world 1, rank 0, full ranges).

@@ -262,6 +262,16 @@ class CudaDenseSession:
     def reset(self) -> None:
         check(_lib.lib().satori_session_reset(self.handle), "reset")
 
+    def rewind(self, position: int) -> None:
+        """Drops the positions at and after `position`; the earlier cached K/V stay."""
+        check(_lib.lib().satori_session_rewind(self.handle, int(position)), "rewind")
+
+    def info(self) -> dict:
+        """kernels per decode step, weight bytes held here, K/V bytes per cached position."""
+        k, w, kv = C.c_int(), C.c_size_t(), C.c_size_t()
+        check(_lib.lib().satori_session_info(self.handle, C.byref(k), C.byref(w), C.byref(kv)), "info")
+        return {"kernels_per_step": k.value, "weight_bytes": w.value, "kv_bytes_per_position": kv.value}
+
     def dispose(self) -> None:
         if self._h:
             _lib.lib().satori_session_destroy(self._h)

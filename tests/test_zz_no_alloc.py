@@ -3,9 +3,15 @@
 Some hosts cannot let a library call cudaMalloc (their pool already owns the GPU's memory, or the
 implied device-wide synchronisation is unacceptable), so satori_grouped_attention_noalloc keeps its
 split-K scratch in a fixed array inside the library.  This test calls it through the C ABI, twice in
-a row on different inputs, and checks each result against satori_grouped_attention_device (which
-uses a context-owned scratch buffer) within the attention tolerance used throughout the suite,
-1e-5 relative + 1e-6 absolute.  It also checks that a shape too large for the fixed array is refused.
+a row on different inputs for each kernel family (the TMA streaming kernel at head_dim 128 with 7
+query heads per KV head, and the plain-load partial kernel at head_dim 64), and checks:
+
+* each result equals satori_grouped_attention_device's bit for bit (same kernels, same split count;
+  only the scratch buffer differs);
+* the first call of each family is within the attention tolerance used throughout the suite,
+  1e-5 relative + 1e-6 absolute, of the oracle's FP64 GroupedAttention;
+* warm calls leave the device's free memory unchanged (they allocate nothing);
+* a shape too large for the fixed array is refused.
 
 The file name makes pytest collect it last, so a run that stops at the first failure has already
 run every other test; it also passes on its own in a fresh process.
@@ -37,13 +43,13 @@ def _inputs(torch, seed, qh, kvh, hd, T):
     return q, k, v
 
 
-def test_noalloc_matches_context_entry_point_twice(env):
+@pytest.mark.parametrize("qh,kvh,hd", [(28, 4, 128), (8, 8, 64)])
+def test_noalloc_matches_context_entry_point_twice(env, oracle_lib, qh, kvh, hd):
     sat, _lib, torch = env
     L = _lib.lib()
     ctx = sat.Context(0)
-    qh, kvh, hd = 28, 4, 128
     for call, T in enumerate((4096, 777)):
-        q, k, v = _inputs(torch, 100 + call, qh, kvh, hd, T)
+        q, k, v = _inputs(torch, 100 + call + hd, qh, kvh, hd, T)
         out_noalloc = torch.full((qh * hd,), float("nan"), device="cuda")
         out_ref = torch.full((qh * hd,), float("nan"), device="cuda")
         torch.cuda.synchronize()
@@ -54,11 +60,35 @@ def test_noalloc_matches_context_entry_point_twice(env):
         _lib.check(L.satori_grouped_attention_device(ctx.handle, q.data_ptr(), k.data_ptr(), v.data_ptr(), qh, kvh,
                                                      hd, T, out_ref.data_ptr()), "device")
         ctx.synchronize()
-        a = out_noalloc.cpu().numpy().astype(np.float64)
-        b = out_ref.cpu().numpy().astype(np.float64)
+        a = out_noalloc.cpu().numpy()
+        b = out_ref.cpu().numpy()
         assert np.all(np.isfinite(a)), call
-        assert np.all(np.abs(a - b) <= TOL_REL * np.abs(b) + TOL_ABS), (call, float(np.abs(a - b).max()))
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), (call, float(np.abs(a - b).max()))
+        if call == 0:
+            ref = oracle_lib.grouped_attention(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), qh, kvh, hd, T,
+                                               threads=8).astype(np.float64)
+            err = np.abs(a.astype(np.float64) - ref)
+            assert np.all(err <= TOL_REL * np.abs(ref) + TOL_ABS), float(err.max())
     ctx.close()
+
+
+def test_noalloc_allocates_nothing(env):
+    sat, _lib, torch = env
+    L = _lib.lib()
+    qh, kvh, hd, T = 28, 4, 128, 2048
+    q, k, v = _inputs(torch, 7, qh, kvh, hd, T)
+    out = torch.empty(qh * hd, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(L.satori_grouped_attention_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), qh, kvh, hd, T,
+                                                  out.data_ptr(), stream), "noalloc warm-up")
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        _lib.check(L.satori_grouped_attention_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), qh, kvh, hd, T,
+                                                      out.data_ptr(), stream), "noalloc")
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert free_after == free_before
 
 
 def test_noalloc_rejects_shapes_beyond_its_fixed_scratch(env):
