@@ -1,23 +1,36 @@
 """Benchmark of the Satori decode hot path on B200 (one JSON line on rank 0).
 
-Default workload (the configuration its MatVec metric is quoted on):
-one step = one GGUF Q8_0 4096x4096 MatVec plus one Q4_0 11008x4096 MatVec in the decode
-(ExecuteBatch) order, over seeded N(0, 0.02^2) weights and an N(0,1) input.  The step rotates
-through enough distinct weight copies that the timed working set (several times the 126 MB L2)
-streams from HBM on every launch.  value = payload GB/s (weights incl. scales).
+Default workload -- BASELINE.json's decode metric, configs[4]: greedy decode of the Qwen2-style 7B
+shape (hidden 3584, 28 layers, 28/4 heads x 128, FFN 18944, vocab 152064; Q4_0 projections, Q8_0
+embedding and lm_head, seeded N(0, 0.02^2) weights quantized on the device).  A 2048-token random
+prompt is cached once; one step = 256 greedy tokens decoded from that context (the session is
+rewound to position 2048 before every step, so every step decodes the same positions).
+value = tokens/s of the whole job.
 
---gpus N (torchrun): weak scaling; every rank processes its own independent matrices (no
-data-path collective; the path shards by object); value = all ranks' bytes / max-over-ranks time.
+--gpus N (torchrun, one process per GPU): the same model row-sharded over N GPUs (every projection
+split by rows, attention by query heads, vectors all-gathered over NVLink inside the step graph):
+strong scaling, value = tokens / max-over-ranks device time.
 
-Other workloads (for the profiles and the design tables): --workload attention | ternary | decode7b |
-decode1p5b.  --impl reference times the reference's CPU path (the C restatement of
-ExecuteBatchFloat, all host threads) on the same config and metric.
+Before timing, at every N, a short parity check runs the session on the same 7B tensors for 4 prompt
+tokens + 4 greedy tokens and compares every step's logits (1e-4 relative + 1e-5 absolute) and greedy
+token (identical) with the CPU oracle's DenseSession restatement; the line carries the result.
+
+At N = 1 the line also carries `kernels` (each hot kernel alone, >= 5 repeats of >= 0.5 s regions,
+min / median / spread): configs[1] MatVec, configs[2] attention at T = 512 / 4096 / 32768 and
+configs[0] Ternary2 4096^2 at block 64 / 128 / 256; and `cpu_baseline`: the oracle's decode step on
+the host cores at the same context, all threads and one thread.
+
+--impl reference times the reference's CPU path (the oracle's C restatement of DenseSession.Append,
+all host threads; the C# reference cannot run in this image) on the same metric and config.
+Other workloads, for profiling one kernel: --workload matvec | attention | ternary | decode1p5b.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -30,6 +43,7 @@ sys.path.insert(0, ROOT)
 import numpy as np  # noqa: E402
 
 GB = 1e9
+LOGIT_REL, LOGIT_ABS = 1e-4, 1e-5      # stated tolerance on logits after a full decode step
 
 
 def _peaks():
@@ -39,6 +53,17 @@ def _peaks():
         return float(p["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def _cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
 
 
 # ------------------------------------------------------------------ clocks sampler
@@ -149,148 +174,85 @@ def device_quantized(ctx, rows, cols, fmt, seed, sigma=0.02):
     return out
 
 
-def events_time(fn, stream, steps: int) -> float:
-    """Device time (ms) of `steps` calls of fn() bracketed by CUDA events on `stream`."""
+def events_time(fn, stream, calls: int) -> float:
+    """Device time (ms) of `calls` calls of fn() bracketed by CUDA events on `stream`."""
     import torch
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):  # CUDAGraph.replay() launches on the current stream
         start.record(stream)
-        for _ in range(steps):
+        for _ in range(calls):
             fn()
         end.record(stream)
     torch.cuda.synchronize()
     return start.elapsed_time(end)
 
 
-# ------------------------------------------------------------------ MatVec workload (configs[1])
+def repeat_regions(replay, stream, units_per_replay: int, min_region_s: float = 0.5, repeats: int = 5):
+    """ms per unit over `repeats` timed regions of >= min_region_s each (replays of one CUDA graph)."""
+    ms1 = max(events_time(replay, stream, 1), 1e-3)
+    n = max(1, int(math.ceil(min_region_s * 1e3 / ms1)))
+    return [events_time(replay, stream, n) / (n * units_per_replay) for _ in range(repeats)]
+
+
+def stats_record(bytes_per_unit: float, ms_list, peak: float, peak_kind: str, extra=None):
+    """GB/s record from per-unit times: best (min time), median and spread, with the roofline fraction."""
+    best, med = min(ms_list), statistics.median(ms_list)
+    rec = {"value": round(bytes_per_unit / (best / 1e3) / GB, 1),
+           "median": round(bytes_per_unit / (med / 1e3) / GB, 1), "unit": "GB/s",
+           "spread": round((max(ms_list) - best) / best, 4), "repeats": len(ms_list),
+           "us_per_unit_min": round(best * 1e3, 3), "algorithmic_bytes_per_unit": bytes_per_unit,
+           "frac": round(bytes_per_unit / (best / 1e3) / GB / peak, 4), "peak": peak, "peak_kind": peak_kind}
+    if extra:
+        rec.update(extra)
+    return rec
+
+
+# ------------------------------------------------------------------ kernel measurements (N = 1)
 MATVEC_SHAPES = [(0, 4096, 4096), (1, 11008, 4096)]
-MATVEC_METRIC = "MatVec payload GB/s (GGUF Q8_0 4096x4096 + Q4_0 11008x4096, decode ExecuteBatch order)"
-MATVEC_WORKLOAD = "configs[1]: GGUF Q8_0 4096x4096 and Q4_0 11008x4096 MatVec"
-# dram__bytes_read.sum + dram__bytes_write.sum per launch, averaged over the two kernels, from one ncu
-# capture of this workload (Q8_0 17,875,712 + Q4_0 25,412,352 bytes; profiles/gemv_rows_matvec_bench.md).
-MATVEC_NCU_TRAFFIC = (17875712 + 25412352) / 2
 
 
-def bench_matvec(args, rank, world, local):
+def kernel_matvec(ctx, stream, copies=12, **kw):
+    """one Q8_0 4096x4096 + one Q4_0 11008x4096 MatVec (decode order) per unit, rotating
+    `copies` distinct weight copies (working set > 4x L2)."""
     import torch
 
     import satori_b200 as sat
     from satori_b200 import _lib
-    ctx = sat.Context(local)
-    step_bytes = sum(r * (c // 32) * (34 if f == 0 else 18) for f, r, c in MATVEC_SHAPES)
-    copies = max(1, int(args.copies))
     mats = []
     for c in range(copies):
         for fmt, rows, cols in MATVEC_SHAPES:
-            dev = device_quantized(ctx, rows, cols, fmt, seed=1000 * rank + 10 * c + fmt)
+            dev = device_quantized(ctx, rows, cols, fmt, seed=10 * c + fmt)
             mats.append(sat.CudaQuantizedMatrix.from_device(ctx, dev.data_ptr(), dev.numel(), rows, cols, fmt))
             del dev
-    gen = torch.Generator(device="cuda").manual_seed(77)
-    x = torch.randn(4096, generator=gen, device="cuda", dtype=torch.float32)
-    y = torch.empty(11008, device="cuda", dtype=torch.float32)
+    x = torch.randn(4096, generator=torch.Generator(device="cuda").manual_seed(77), device="cuda")
+    y = torch.empty(11008, device="cuda")
     torch.cuda.synchronize()
-    stream = torch.cuda.Stream()
     ctx.set_stream(stream.cuda_stream)
-
-    def one_step(i):
-        for k in range(2):
-            mats[2 * (i % copies) + k].execute_device(x.data_ptr(), y.data_ptr(), 1, _lib.ORDER_BATCH)
-
-    # Warm-up outside capture, then capture the rotation (copies steps) into one CUDA graph.
     with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            one_step(i)
+        for m in mats:
+            m.execute_device(x.data_ptr(), y.data_ptr(), 1, _lib.ORDER_BATCH)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        for i in range(copies):
-            one_step(i)
+        for m in mats:
+            m.execute_device(x.data_ptr(), y.data_ptr(), 1, _lib.ORDER_BATCH)
     torch.cuda.synchronize()
-    for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize()
-    replays = max(1, args.steps // copies)
-    steps = replays * copies
-    dist_barrier(world)
-    with ClockSampler(local) as clocks:
-        ms = events_time(graph.replay, stream, replays)
-    ms = dist_max(ms, world)
-    launches = steps * 2
-    value = step_bytes * steps * world / (ms / 1e3) / GB
-    achieved = step_bytes * steps / (ms / 1e3) / GB   # per GPU: the kernel's algorithmic bytes / device time
-
-    # e2e through the public C ABI with host buffers: H2D x, MatVec, D2H y per call (pinned staging).
+    ms = repeat_regions(graph.replay, stream, copies, **kw)
     ctx.set_stream(None)
-    xh = np.random.default_rng(5).standard_normal(4096).astype(np.float32)
-    for m in mats:
-        m.execute_batch(xh, 1)
-    e2e_steps = max(4, min(steps, 200))
-    dist_barrier(world)
-    t0 = time.perf_counter()
-    for i in range(e2e_steps):
-        for k in range(2):
-            mats[2 * (i % copies) + k].execute_batch(xh, 1)
-    e2e_s = dist_max(time.perf_counter() - t0, world)
-    e2e_value = step_bytes * e2e_steps * world / e2e_s / GB
-    peak, peak_kind = _peaks()
-    result = {
-        "metric": MATVEC_METRIC,
-        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
-        "ms_per_step": round(ms / steps, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "q8_0/q4_0 weights, f32 activations and accumulation",
-        "data": "synthetic: seeded N(0,0.02^2) weights quantized on the device, N(0,1) input",
-        "config": {"workload": MATVEC_WORKLOAD,
-                   "order": "ExecuteBatch (decode) FP32 order, bit-exact to the reference",
-                   "weight_copies_rotated": copies, "working_set_MB": round(step_bytes * copies / 1e6, 1),
-                   "l2_policy": "inputs larger than L2: rotating distinct weight copies",
-                   "parallelism": f"replicas x{world} (independent matrices per rank)"},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": MATVEC_NCU_TRAFFIC, "traffic_source": "profiles/gemv_rows_matvec_bench.md",
-                     "algorithmic_bytes_per_launch": step_bytes / 2},
-        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": 2 * 4096 * 4,
-                "d2h_bytes_per_step": (4096 + 11008) * 4},
-        "gpu_launches": launches,
-        "clocks": clocks.summary(),
-    }
+    step_bytes = sum(r * (c // 32) * (34 if f == 0 else 18) for f, r, c in MATVEC_SHAPES)
+    del graph
     for m in mats:
         m.dispose()
-    return result
+    return step_bytes, ms
 
 
-def cpu_baseline_matvec(budget_s: float = 10.0):
-    """The C restatement of ExecuteBatchFloat + Dot (AVX2+FMA) on all host threads, bounded sample."""
-    from oracle import oracle
-    threads = os.cpu_count() or 1
-    rng = np.random.default_rng(3)
-    data = []
-    for fmt, rows, cols in MATVEC_SHAPES:
-        w = rng.standard_normal(rows * cols, dtype=np.float32) * np.float32(0.02)
-        data.append((oracle.q_quantize(w, rows, cols, fmt), rows, cols, fmt))
-    x = rng.standard_normal(4096).astype(np.float32)
-    step_bytes = sum(p.size for p, *_ in data)
-    for p, r, c, f in data:
-        oracle.q_matvec(p, r, c, f, x, order="batch", threads=threads)
-    n, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < budget_s:
-        for p, r, c, f in data:
-            oracle.q_matvec(p, r, c, f, x, order="batch", threads=threads)
-        n += 1
-    dt = time.perf_counter() - t0
-    return {"value": round(step_bytes * n / dt / GB, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{n} steps (Q8_0 4096x4096 + Q4_0 11008x4096, ExecuteBatchFloat order) in {dt:.1f}s"}
-
-
-# ------------------------------------------------------------------ attention workload (configs[2])
-def bench_attention(args, rank, world, local):
+def kernel_attention(ctx, stream, T, **kw):
+    """GQA 28/4 x 128 over T cached tokens (stream + merge launches), rotating layers."""
     import torch
 
-    import satori_b200 as sat
     from satori_b200 import _lib
-    ctx = sat.Context(local)
     qh, kvh, hd = 28, 4, 128
-    T = int(args.tokens)
     kv_bytes = 2 * T * kvh * hd * 4
     layers = max(2, int(np.ceil(4 * 126e6 / kv_bytes)))
     gen = torch.Generator(device="cuda").manual_seed(9)
@@ -299,63 +261,39 @@ def bench_attention(args, rank, world, local):
     q = torch.randn(qh * hd, generator=gen, device="cuda")
     out = torch.empty(qh * hd, device="cuda")
     torch.cuda.synchronize()
-    stream = torch.cuda.Stream()
     ctx.set_stream(stream.cuda_stream)
     L = _lib.lib()
 
     def call(i):
-        _lib.check(L.satori_grouped_attention_device(ctx.handle, q.data_ptr(), kc[i % layers].data_ptr(),
-                                                     vc[i % layers].data_ptr(), qh, kvh, hd, T, out.data_ptr()))
+        _lib.check(L.satori_grouped_attention_device(ctx.handle, q.data_ptr(), kc[i].data_ptr(), vc[i].data_ptr(),
+                                                     qh, kvh, hd, T, out.data_ptr()))
 
     with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            call(i)
+        call(0)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         for i in range(layers):
             call(i)
-    graph.replay()
     torch.cuda.synchronize()
-    replays = max(1, args.steps // layers)
-    dist_barrier(world)
-    with ClockSampler(local) as clocks:
-        ms = events_time(graph.replay, stream, replays)
-    ms = dist_max(ms, world)
-    steps = replays * layers
-    per = ms / steps
-    peak, peak_kind = _peaks()
-    achieved = kv_bytes / (per / 1e3) / GB
-    return {
-        "metric": f"decode attention K+V GB/s (28q/4kv x 128, T={T})",
-        "value": round(kv_bytes * steps * world / (ms / 1e3) / GB, 2), "unit": "GB/s",
-        "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(per, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic N(0,1) q/k/v",
-        "config": {"workload": f"configs[2]: GQA 28/4 x 128, T={T}", "layers_rotated": layers},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
-                     "algorithmic_bytes_per_launch": kv_bytes},
-        "gpu_launches": steps * 2, "clocks": clocks.summary(),
-    }
+    ms = repeat_regions(graph.replay, stream, layers, **kw)
+    ctx.set_stream(None)
+    del graph, kc, vc
+    return kv_bytes, ms, layers
 
 
-# ------------------------------------------------------------------ Ternary2 workload
-def bench_ternary(args, rank, world, local):
+def kernel_ternary(ctx, stream, n, bs, order="execute", **kw):
+    """Ternary2 n x n MatVec, block bs, N(0,1) weights, rotating copies (> 4x L2)."""
     import torch
 
     import satori_b200 as sat
     from satori_b200 import _lib
     from satori_b200.core import ternary2_byte_length
-    ctx = sat.Context(local)
-    n, bs = int(args.n), int(args.block)
     nbytes = ternary2_byte_length(n, n, bs)
     copies = max(4, int(np.ceil(4 * 126e6 / nbytes)))
-    base = []
     rng = np.random.default_rng(1)
     w = rng.standard_normal(n * n).astype(np.float32)
-    for c in range(4):
-        base.append(sat.Ternary2Matrix.quantize(np.roll(w, c * 7919), n, n, bs, ctx=ctx).device)
+    base = [sat.Ternary2Matrix.quantize(np.roll(w, c * 7919), n, n, bs, ctx=ctx).device for c in range(4)]
     mats = list(base)
     while len(mats) < copies:
         src = base[len(mats) % 4]
@@ -363,37 +301,44 @@ def bench_ternary(args, rank, world, local):
     x = torch.randn(n, device="cuda")
     y = torch.empty(n, device="cuda")
     torch.cuda.synchronize()
-    stream = torch.cuda.Stream()
     ctx.set_stream(stream.cuda_stream)
-    order = _lib.ORDER_EXECUTE if args.order == "execute" else _lib.ORDER_SCALAR
+    o = _lib.ORDER_EXECUTE if order == "execute" else _lib.ORDER_SCALAR
     with torch.cuda.stream(stream):
-        for m in mats[:args.warmup]:
-            m.execute_device(x.data_ptr(), y.data_ptr(), 1, order)
+        mats[0].execute_device(x.data_ptr(), y.data_ptr(), 1, o)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         for m in mats:
-            m.execute_device(x.data_ptr(), y.data_ptr(), 1, order)
-    graph.replay()
+            m.execute_device(x.data_ptr(), y.data_ptr(), 1, o)
     torch.cuda.synchronize()
-    replays = max(1, args.steps // copies)
-    dist_barrier(world)
-    with ClockSampler(local) as clocks:
-        ms = events_time(graph.replay, stream, replays)
-    ms = dist_max(ms, world)
-    steps = replays * copies
-    per = ms / steps
-    peak, peak_kind = _peaks()
-    achieved = nbytes / (per / 1e3) / GB
-    return {"metric": f"Ternary2 MatVec payload GB/s ({n}x{n}, block {bs}, {args.order} order)",
-            "value": round(nbytes * steps * world / (ms / 1e3) / GB, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": steps, "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "ternary2 weights, f32", "data": "synthetic N(0,1)",
-            "config": {"workload": f"configs[0]: Ternary2 {n}^2 bs{bs}", "copies": copies},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
-                         "algorithmic_bytes_per_launch": nbytes},
-            "gpu_launches": steps, "clocks": clocks.summary()}
+    ms = repeat_regions(graph.replay, stream, copies, **kw)
+    ctx.set_stream(None)
+    del graph
+    for m in mats:
+        m.dispose()
+    return nbytes, ms, copies
+
+
+def kernels_record(ctx, min_region_s=0.5, repeats=5):
+    import torch
+    peak, kind = _peaks()
+    stream = torch.cuda.Stream()
+    kw = dict(min_region_s=min_region_s, repeats=repeats)
+    out = {}
+    b, ms = kernel_matvec(ctx, stream, **kw)
+    out["matvec_q8_0_4096x4096+q4_0_11008x4096"] = stats_record(
+        b, ms, peak, kind, {"workload": "configs[1]", "launches_per_unit": 2,
+                            "order": "ExecuteBatch (decode), bit-exact"})
+    for T in (512, 4096, 32768):
+        b, ms, layers = kernel_attention(ctx, stream, T, **kw)
+        out[f"attention_T{T}"] = stats_record(b, ms, peak, kind, {"workload": f"configs[2] 28/4 x 128, T={T}",
+                                                                  "layers_rotated": layers})
+    for bs in (64, 128, 256):
+        b, ms, copies = kernel_ternary(ctx, stream, 4096, bs, **kw)
+        out[f"ternary2_4096x4096_bs{bs}"] = stats_record(b, ms, peak, kind,
+                                                         {"workload": f"configs[0] bs{bs}", "copies": copies,
+                                                          "order": "Ternary2Avx2Kernel, bit-exact"})
+    return out
 
 
 # ------------------------------------------------------------------ decode workloads
@@ -411,12 +356,107 @@ def device_model(ctx, spec, seed):
     return tensors
 
 
-def bench_decode(args, rank, world, local, spec):
+def decode_parity(sess, spec, tensors, rank, n_prompt=4, n_gen=4):
+    """Every rank steps the session; rank 0 replays the same tokens through the oracle and compares."""
+    prompt = [int(t) for t in np.random.default_rng(11).integers(0, spec.vocab, n_prompt)]
+    feed, logits, greedy = [], [], []
+    tok = None
+    for i in range(n_prompt + n_gen):
+        t = prompt[i] if i < n_prompt else tok
+        lg, tok = sess.append(t)
+        feed.append(t)
+        logits.append(lg)
+        greedy.append(tok)
+    sess.reset()
+    if rank != 0:
+        return None, None
+    from oracle.oracle import OracleSession
+    host = {k: v.cpu().numpy() for k, v in tensors.items()}
+    ref = OracleSession(spec, host, n_prompt + n_gen + 1)
+    threads = os.cpu_count() or 1
+    worst, tokens_ok, logits_ok = 0.0, True, True
+    for i, t in enumerate(feed):
+        lr, ar = ref.append(t, threads=threads)
+        err = np.abs(logits[i].astype(np.float64) - lr)
+        bound = LOGIT_REL * np.abs(lr) + LOGIT_ABS
+        worst = max(worst, float(np.max(err / bound)))
+        logits_ok &= bool(np.all(err <= bound))
+        tokens_ok &= ar == greedy[i]
+    ref.close()
+    rec = {"ok": bool(tokens_ok and logits_ok), "steps": len(feed), "greedy_tokens_identical": bool(tokens_ok),
+           "logits_within_tol": bool(logits_ok), "tolerance": f"{LOGIT_REL} rel + {LOGIT_ABS} abs",
+           "worst_err_over_bound": round(worst, 4), "against": "oracle DenseSession restatement (CPU)"}
+    return rec, host
+
+
+def cpu_decode_rate(spec, host, context, threads, min_s, min_tokens, max_tokens, cache_seed=5):
+    """The oracle's DenseSession.Append at position `context` (synthetic cache rows), host cores."""
+    from oracle.oracle import OracleSession
+    ref = OracleSession(spec, host, context + max_tokens + 1)
+    ref.fill_cache(context, cache_seed)
+    ref.append(1, threads=threads)                 # warm-up (page-in)
+    n, t0 = 0, time.perf_counter()
+    while n < max_tokens and (n < min_tokens or time.perf_counter() - t0 < min_s):
+        ref.append(1 + n, threads=threads)
+        n += 1
+    dt = time.perf_counter() - t0
+    ref.close()
+    return n / dt, n, dt
+
+
+def host_random_model(spec, seed):
+    """Payloads cut from one seeded 16 MiB random pattern, with finite fp16 scales written into every
+    block (timing only: decode cost does not depend on the values), and the model's float vectors;
+    built on the host without the GPU."""
+    rng = np.random.default_rng(seed)
+    pattern = np.frombuffer(rng.bytes(1 << 24), dtype=np.uint8)
+    host = {}
+    for i, (name, (rows, cols)) in enumerate(spec.matrix_shapes().items()):
+        fmt = spec.format_of(name)
+        bb = 34 if fmt == 0 else 18
+        nblk = rows * (cols // 32)
+        flat = np.empty(nblk * bb, dtype=np.uint8)
+        src = np.roll(pattern, 4099 * i)
+        for off in range(0, flat.size, src.size):
+            flat[off:off + src.size] = src[:flat.size - off]
+        buf = flat.reshape(nblk, bb)
+        scale = np.float16(0.02 / (127.0 if fmt == 0 else 8.0))
+        buf[:, 0:2] = np.frombuffer(scale.tobytes(), dtype=np.uint8)
+        host[name] = flat
+    for name, n in spec.vector_shapes().items():
+        host[name] = ((1.0 if name.endswith("norm.weight") else 0.0) +
+                      0.02 * rng.standard_normal(n)).astype(np.float32)
+    return host
+
+
+def cpu_baseline_decode(spec, host, context):
+    all_threads = os.cpu_count() or 1
+    v_all, n_all, dt_all = cpu_decode_rate(spec, host, context, all_threads, min_s=8.0, min_tokens=3,
+                                           max_tokens=64)
+    v_one, n_one, dt_one = cpu_decode_rate(spec, host, context, 1, min_s=5.0, min_tokens=1, max_tokens=8)
+    return {"value": round(v_all, 4), "unit": "tokens/s", "cores": all_threads, "kind": "port",
+            "sample": f"{n_all} decode steps at context {context} in {dt_all:.1f}s (oracle DenseSession.Append "
+                      f"restatement, AVX2/FMA, OpenMP row split, synthetic cache rows)",
+            "single_thread": {"value": round(v_one, 4), "unit": "tokens/s", "cores": 1,
+                              "sample": f"{n_one} decode steps in {dt_one:.1f}s"},
+            "cpu_model": _cpu_model()}
+
+
+def _embedding_table_bytes(spec, world):
+    """Bytes of token_embd.weight inside a session's weight bytes that a step does not stream (a step
+    reads one row): the whole table, unless it is also the single-GPU output matrix."""
+    if spec.tied_embeddings and world == 1:
+        return 0
+    return spec.vocab * (spec.hidden // 32) * 34
+
+
+def bench_decode(args, rank, world, local, spec, with_kernels: bool):
     import torch
 
     import satori_b200 as sat
     ctx = sat.Context(local)
-    context = args.prompt + args.decode + 8
+    P, D = args.prompt, args.decode
+    context = P + D + 8
     tensors = device_model(ctx, spec, seed=31)
     torch.cuda.synchronize()
     if world == 1:
@@ -424,98 +464,174 @@ def bench_decode(args, rank, world, local, spec):
     else:
         sess = sat.CudaDenseSession(spec, tensors, context, ctx=ctx, rank=rank, world=world,
                                     nccl_id=sat.broadcast_nccl_id())
+    info = sess.info()
+    parity, host = decode_parity(sess, spec, tensors, rank)
     del tensors
     torch.cuda.empty_cache()
-    prompt = np.random.default_rng(4).integers(0, spec.vocab, args.prompt).astype(np.int32)
+    dist_barrier(world)
+
+    prompt = np.random.default_rng(4).integers(0, spec.vocab, P).astype(np.int32)
     last = sess.prefill(prompt)
+    for _ in range(args.warmup):
+        sess.rewind(P)
+        ref_tokens = sess.generate(int(last), D)
     ext = torch.cuda.ExternalStream(ctx.stream)
     torch.cuda.synchronize()
     dist_barrier(world)
+    stable = True
     with ClockSampler(local) as clocks:
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(ext)
         t0 = time.perf_counter()
-        toks = sess.generate(int(last), args.decode)
+        for _ in range(args.steps):
+            sess.rewind(P)
+            toks = sess.generate(int(last), D)
+            stable &= bool(np.array_equal(toks, ref_tokens))
         wall = time.perf_counter() - t0
         end.record(ext)
         torch.cuda.synchronize()
     ms = dist_max(start.elapsed_time(end), world)
-    tps = args.decode / (ms / 1e3)
-    wbytes = spec.weight_bytes(include_embedding_table=False) + spec.hidden // 32 * 34
-    kv_avg = 2 * spec.layers * spec.kv_width * 4 * (args.prompt + args.decode / 2)
-    # Per GPU: a 1/world row share of every matrix and the KV heads of this rank's query heads.
-    achieved = (wbytes + kv_avg) / world / (ms / 1e3 / args.decode) / GB
+    wall = dist_max(wall, world)
+    tokens = args.steps * D
+    tps = tokens / (ms / 1e3)
+    # Per GPU and token: this rank's weight rows, one embedding row, and the cached K/V it reads.
+    kv_avg = info["kv_bytes_per_position"] * (P + D / 2)
+    bytes_per_token = (info["weight_bytes"] - _embedding_table_bytes(spec, world) + spec.hidden // 32 * 34
+                       + kv_avg)
+    achieved = bytes_per_token / (ms / 1e3 / tokens) / GB
     peak, peak_kind = _peaks()
-    return {"metric": f"decode tokens/s ({spec.name})", "value": round(tps, 2), "unit": "tokens/s",
-            "n_gpus": world, "steps": args.decode, "warmup": args.prompt, "ms_per_step": round(ms / args.decode, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "quantized weights, f32 activations", "data": "synthetic seeded weights, random prompt",
-            "config": {"workload": spec.name, "prompt": args.prompt, "decode": args.decode,
-                       "parallelism": "single GPU" if world == 1 else
-                       f"tp{world}: row-sharded projections, query-head-sharded attention, all-gathers",
-                       "exchange": None if world == 1 else os.environ.get("SATORI_EXCHANGE", "p2p")},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
-                         "algorithmic_bytes_per_launch": wbytes + kv_avg},
-            "e2e": {"value": round(args.decode / wall, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
-                    "d2h_bytes_per_step": 4},
-            "first_tokens": [int(t) for t in toks[:8]], "clocks": clocks.summary()}
+    res = {
+        "metric": f"decode tokens/s ({spec.name}, {P}-token context, {D} greedy tokens per step)",
+        "value": round(tps, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "ms_per_token": round(ms / tokens, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "q4_0/q8_0 weights, f32 activations and accumulation",
+        "data": "synthetic: seeded N(0,0.02^2) weights quantized on the device, seeded random prompt",
+        "config": {"workload": f"configs[{4 if spec.name.startswith('qwen2-7b') else 3}]: {spec.name}",
+                   "context": P, "decode_tokens_per_step": D,
+                   "l2_policy": "inputs larger than L2: every token streams all weights (GBs) from HBM",
+                   "parallelism": "single GPU" if world == 1 else
+                   f"tp{world}: row-sharded projections, query-head-sharded attention, in-graph all-gathers",
+                   "exchange": None if world == 1 else os.environ.get("SATORI_EXCHANGE", "p2p")},
+        "parity": parity,
+        "deterministic_steps": stable,
+        "roofline": {"bound": "hbm", "unit_of_work": "one decode token (every launch of the step, this GPU)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_token": int(bytes_per_token)},
+        "e2e": {"value": round(tokens / wall, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": 4 * D + 28,
+                "api": "satori_session_rewind + satori_session_generate (host token in, host tokens out)"},
+        "gpu_launches": info["kernels_per_step"] * tokens,
+        "launches_per_token": info["kernels_per_step"],
+        "first_tokens": [int(t) for t in ref_tokens[:8]],
+        "clocks": clocks.summary(),
+    }
+    sess.dispose()
+    if with_kernels and rank == 0 and world == 1:
+        res["kernels"] = kernels_record(ctx)
+    if rank == 0 and world == 1 and host is not None and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline_decode(spec, host, P)
+    return res
+
+
+# ------------------------------------------------------------------ single-kernel workloads (profiling)
+def bench_kernel(args, local):
+    import torch
+
+    import satori_b200 as sat
+    ctx = sat.Context(local)
+    stream = torch.cuda.Stream()
+    peak, kind = _peaks()
+    kw = dict(min_region_s=args.region, repeats=args.repeats)
+    if args.workload == "matvec":
+        b, ms = kernel_matvec(ctx, stream, **kw)
+        name, launches = "configs[1] MatVec Q8_0 4096^2 + Q4_0 11008x4096", 2
+    elif args.workload == "attention":
+        b, ms, _ = kernel_attention(ctx, stream, args.tokens, **kw)
+        name, launches = f"configs[2] attention T={args.tokens}", 2
+    else:
+        b, ms, _ = kernel_ternary(ctx, stream, args.n, args.block, args.order, **kw)
+        name, launches = f"configs[0] Ternary2 {args.n}^2 bs{args.block}", 1
+    rec = stats_record(b, ms, peak, kind)
+    return {"metric": f"{name} payload GB/s", "value": rec["value"], "unit": "GB/s", "n_gpus": 1,
+            "higher_is_better": True, "kernel": rec, "gpu_launches_per_unit": launches}
 
 
 # ------------------------------------------------------------------ reference arm
-def reference_arm(args, rank, world):
+def reference_arm(args, rank, world, spec):
     if rank != 0:
         return None
-    base = cpu_baseline_matvec(budget_s=max(3.0, min(20.0, 0.05 * args.steps)))
-    return {"metric": MATVEC_METRIC, "value": base["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "impl": "reference", "dtype": "q8_0/q4_0 weights, f32", "data": "synthetic seeded",
-            "config": {"workload": MATVEC_WORKLOAD,
-                       "implementation": "C restatement of QuantizedMatVec.ExecuteBatchFloat/Dot (AVX2+FMA), all "
-                                         "host threads (the C# reference cannot be built in this image)"},
-            "cpu_baseline": base, "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
-                                          "d2h_bytes_per_step": 0}}
+    P = args.prompt
+    host = host_random_model(spec, seed=3)
+    threads = os.cpu_count() or 1
+    from oracle.oracle import OracleSession
+    ref = OracleSession(spec, host, P + args.warmup + args.steps + 2)
+    ref.fill_cache(P, 5)
+    for i in range(args.warmup):
+        ref.append(1 + i, threads=threads)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        ref.append(100 + i, threads=threads)
+    dt = time.perf_counter() - t0
+    ref.close()
+    tps = args.steps / dt
+    v_one, n_one, dt_one = cpu_decode_rate(spec, host, P, 1, min_s=5.0, min_tokens=1, max_tokens=4)
+    base = {"value": round(tps, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{args.steps} decode steps at context {P} in {dt:.1f}s (one step = one token; synthetic "
+                      f"cache rows; seeded random payloads)",
+            "single_thread": {"value": round(v_one, 4), "unit": "tokens/s", "cores": 1,
+                              "sample": f"{n_one} decode steps in {dt_one:.1f}s"},
+            "cpu_model": _cpu_model()}
+    return {"metric": f"decode tokens/s ({spec.name}, {P}-token context, {args.decode} greedy tokens per step)",
+            "value": round(tps, 4), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "impl": "reference", "dtype": "q4_0/q8_0 weights, f32", "data": "synthetic seeded",
+            "config": {"workload": f"configs[{4 if spec.name.startswith('qwen2-7b') else 3}]: {spec.name}",
+                       "context": P,
+                       "implementation": "C restatement of DenseSession.Append / DenseForward.Step (AVX2+FMA "
+                                         "ExecuteBatchFloat, FP64 attention), all host threads (the C# reference "
+                                         "cannot be built in this image)"},
+            "cpu_baseline": base,
+            "e2e": {"value": round(tps, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=600)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="satori", choices=["satori", "reference"])
-    ap.add_argument("--workload", default="matvec",
-                    choices=["matvec", "attention", "ternary", "decode7b", "decode1p5b"])
-    ap.add_argument("--copies", type=int, default=12)
+    ap.add_argument("--workload", default="decode7b",
+                    choices=["decode7b", "decode1p5b", "matvec", "attention", "ternary"])
     ap.add_argument("--tokens", type=int, default=32768)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--block", type=int, default=128)
     ap.add_argument("--order", default="execute", choices=["execute", "scalar"])
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--decode", type=int, default=256)
+    ap.add_argument("--region", type=float, default=0.5, help="seconds per timed region (kernel workloads)")
+    ap.add_argument("--repeats", type=int, default=5)
+    ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel records of the decode line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    args.steps = max(1, args.steps)
+    import satori_b200 as sat
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))
-        res = reference_arm(args, rank, world)
+        spec = sat.qwen2_1_5b() if args.workload == "decode1p5b" else sat.qwen2_7b()
+        res = reference_arm(args, rank, world, spec)
         if res is not None:
             print(json.dumps(res), flush=True)
         return
     rank, world, local = dist_init()
-    import satori_b200 as sat
-    if args.workload == "matvec":
-        res = bench_matvec(args, rank, world, local)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            res["cpu_baseline"] = cpu_baseline_matvec()
-    elif args.workload == "attention":
-        res = bench_attention(args, rank, world, local)
-    elif args.workload == "ternary":
-        res = bench_ternary(args, rank, world, local)
-    elif args.workload == "decode7b":
-        res = bench_decode(args, rank, world, local, sat.qwen2_7b())
+    if args.workload in ("decode7b", "decode1p5b"):
+        spec = sat.qwen2_7b() if args.workload == "decode7b" else sat.qwen2_1_5b()
+        res = bench_decode(args, rank, world, local, spec, with_kernels=not args.no_kernels)
     else:
-        res = bench_decode(args, rank, world, local, sat.qwen2_1_5b())
+        res = bench_kernel(args, local) if rank == 0 else None
     if rank == 0 and res is not None:
         print(json.dumps(res), flush=True)
     if world > 1:

@@ -1,5 +1,6 @@
-"""bench.py's reference arm (the oracle's CPU restatement of the path, timed on the host) keeps the
-JSON-line contract the driver reads; it needs no GPU, so it is checked here on the CPU."""
+"""bench.py's reference arm (the oracle's CPU restatement of the 7B decode step, timed on the host at
+all threads and at one thread) keeps the JSON-line contract the driver reads; it needs no GPU, so it is
+checked here on the CPU."""
 import json
 import os
 import subprocess
@@ -18,8 +19,9 @@ def test_reference_arm_prints_one_contract_line():
     for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "higher_is_better", "scaling", "vs_baseline",
                 "dtype", "data", "config", "cpu_baseline", "e2e"):
         assert key in d, key
-    assert d["impl"] == "reference" and d["value"] > 0 and d["unit"] == "GB/s"
+    assert d["impl"] == "reference" and d["value"] > 0 and d["unit"] == "tokens/s"
     assert d["warmup"] >= 3 and d["steps"] == 1
     assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["value"] == d["value"] and d["e2e"]["h2d_bytes_per_step"] == 0
-    assert "workload" in d["config"]
+    assert "workload" in d["config"] and d["config"]["workload"].startswith("configs[4]")
+    assert d["cpu_baseline"]["single_thread"]["cores"] == 1 and d["cpu_baseline"]["single_thread"]["value"] > 0

@@ -8,7 +8,9 @@ identical on the small configs").
 import numpy as np
 import pytest
 
-from model_util import synthetic_tensors
+import os
+
+from model_util import device_synthetic_tensors, synthetic_tensors
 
 pytestmark = pytest.mark.gpu
 
@@ -33,12 +35,13 @@ def _run_pair(sat, ctx, spec, prompt, n_gen, context=64, seed=7, tensors=None):
     tensors = tensors if tensors is not None else synthetic_tensors(spec, seed)
     gpu = sat.CudaDenseSession(spec, tensors, context, ctx=ctx)
     ref = OracleSession(spec, tensors, context)
+    threads = max(8, os.cpu_count() or 1)
     tok = None
     greedy = []
     for i in range(len(prompt) + n_gen):
         t = int(prompt[i]) if i < len(prompt) else tok
         lg, ag = gpu.append(t)
-        lr, ar = ref.append(t, threads=8)
+        lr, ar = ref.append(t, threads=threads)
         err = np.abs(lg.astype(np.float64) - lr)
         assert np.all(err <= LOGIT_REL * np.abs(lr) + LOGIT_ABS), (i, float(err.max()))
         assert ag == ar, (i, ag, ar)
@@ -109,12 +112,46 @@ def test_session_errors(sat, ctx, oracle_lib):
         sat.CudaDenseSession(bad, t2, 4, ctx=ctx)
 
 
-def test_qwen2_1_5b_shape_greedy_tokens_identical(sat, ctx, oracle_lib):
-    """BASELINE config 4 shape (28 layers, 1536 hidden, 12/2 heads, vocab 151936, Q8_0): a seeded
-    prompt then greedy decode; every step's greedy token equals the oracle's."""
+def test_qwen2_1_5b_config_128_prompt_256_greedy_tokens_identical(sat, ctx, oracle_lib):
+    """BASELINE config 4 as stated (28 layers, 1536 hidden, 12/2 heads, FFN 8960, vocab 151936, all
+    Q8_0; a 128-token seeded prompt, then 256 greedy tokens): every step's logits are within tolerance
+    of the oracle's and every greedy token is identical (DenseSession.cs:111-131)."""
     spec = sat.qwen2_1_5b()
-    prompt = list(np.random.default_rng(4).integers(0, spec.vocab, 12))
-    _run_pair(sat, ctx, spec, prompt=prompt, n_gen=12, context=32, seed=21)
+    tensors = device_synthetic_tensors(ctx, spec, seed=21)
+    prompt = list(np.random.default_rng(4).integers(0, spec.vocab, 128))
+    gpu, ref, greedy = _run_pair(sat, ctx, spec, prompt=prompt, n_gen=256, context=400, tensors=tensors)
+    assert gpu.position == ref.position == 384
+    gpu.dispose()
+    ref.close()
+
+
+def test_qwen2_7b_shape_session_matches_oracle(sat, ctx, oracle_lib):
+    """BASELINE config 5 shape on one GPU (28 layers, 3584 hidden, 28/4 heads, FFN 18944, vocab
+    152064; Q4_0 projections, Q8_0 embedding and lm_head): 4 prompt tokens + 8 greedy tokens, logits
+    within tolerance and greedy tokens identical to the oracle's at every step."""
+    spec = sat.qwen2_7b()
+    tensors = device_synthetic_tensors(ctx, spec, seed=31)
+    prompt = list(np.random.default_rng(8).integers(0, spec.vocab, 4))
+    gpu, ref, _ = _run_pair(sat, ctx, spec, prompt=prompt, n_gen=8, context=16, tensors=tensors)
+    gpu.dispose()
+    ref.close()
+
+
+def test_rewind_replays_identically(sat, ctx, oracle_lib):
+    """satori_session_rewind keeps the cache below the position: decoding again from there gives the
+    same tokens bitwise, and a rewind past the committed position is refused."""
+    spec = sat.tiny()
+    s = sat.CudaDenseSession(spec, synthetic_tensors(spec, 13), 64, ctx=ctx)
+    s.prefill([5, 9, 17, 2])
+    first = s.generate(7, 12)
+    s.rewind(4)
+    again = s.generate(7, 12)
+    assert list(first) == list(again) and s.position == 16
+    with pytest.raises(sat.ArgumentError):
+        s.rewind(17)
+    info = s.info()
+    assert info["kernels_per_step"] > 0 and info["weight_bytes"] > 0
+    assert info["kv_bytes_per_position"] == spec.layers * 2 * spec.kv_width * 4
 
 
 @pytest.mark.parametrize("fmt", [0, 1])
