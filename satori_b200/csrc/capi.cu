@@ -9,6 +9,7 @@
 #include "gemv.cuh"
 
 #include <math.h>
+#include <stdlib.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -132,6 +133,22 @@ int upload_payload(satori_ctx *ctx, const uint8_t *src, bool src_is_device, size
     return SATORI_OK;
 }
 
+// SATORI_GEMV_STREAM=0 routes every decode MatVec to gemv_rows (both kernels give the same bits).
+bool stream_kernel_enabled()
+{
+    static const bool on = [] {
+        const char *v = getenv("SATORI_GEMV_STREAM");
+        return !(v && strcmp(v, "0") == 0);
+    }();
+    return on;
+}
+
+bool gemv_fused_takes(int rows, int cols, int format, int epilogue, int sm_count, size_t smem_limit)
+{
+    return (stream_kernel_enabled() && gemv_stream_takes(rows, cols, format, epilogue, sm_count, smem_limit)) ||
+           gemv_rows_takes(rows, cols, format, epilogue, sm_count, smem_limit);
+}
+
 int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int format, int order, const float *dx,
              float *dy, int positions, int epilogue, const float *bias, float *residual, cudaStream_t stream,
              int use_pdl, const float *norm_w, float norm_eps, const XPush *xp, const XWait *xw)
@@ -159,7 +176,16 @@ int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int 
             a.norm_eps = norm_eps;
             if (xp) a.xp = *xp;
             if (xw) a.xw = *xw;
-            DecodePlan dp = plan_gemv_rows(a, ctx->sm_count, ctx->smem_optin);
+            DecodePlan dp = {};
+            if (stream_kernel_enabled()) {
+                dp = plan_gemv_stream(a, ctx->sm_count, ctx->smem_optin);
+                if (dp.ok) {
+                    cudaError_t e = launch_gemv_stream(a, dp, stream);
+                    if (e != cudaSuccess) return cuda_fail(e, "launch decode MatVec");
+                    continue;
+                }
+            }
+            dp = plan_gemv_rows(a, ctx->sm_count, ctx->smem_optin);
             if (dp.ok) {
                 cudaError_t e = launch_gemv_rows(a, dp, stream);
                 if (e != cudaSuccess) return cuda_fail(e, "launch decode MatVec");

@@ -57,6 +57,14 @@ DecodePlan plan_gemv_rows(const GemvArgs &a, int sm_count, size_t smem_limit);
 // epilogue and the fused RmsNorm of x).
 bool gemv_rows_takes(int rows, int cols, int format, int epilogue, int sm_count, size_t smem_limit);
 cudaError_t launch_gemv_rows(const GemvArgs &a, const DecodePlan &plan, cudaStream_t stream);
+// gemv_stream.cu: the same order for the decode configurations' row widths with the width fixed at
+// compile time (kind 3); preferred over gemv_rows where it takes the shape.
+DecodePlan plan_gemv_stream(const GemvArgs &a, int sm_count, size_t smem_limit);
+bool gemv_stream_takes(int rows, int cols, int format, int epilogue, int sm_count, size_t smem_limit);
+cudaError_t launch_gemv_stream(const GemvArgs &a, const DecodePlan &plan, cudaStream_t stream);
+// True when one of the two decode row kernels takes the shape (and with it the fused RmsNorm of x, the
+// SwiGLU epilogue and a carried peer exchange).
+bool gemv_fused_takes(int rows, int cols, int format, int epilogue, int sm_count, size_t smem_limit);
 DecodePlan plan_gemv_decode(const GemvArgs &a, int sm_count, size_t smem_limit);
 cudaError_t launch_gemv_decode(const GemvArgs &a, const DecodePlan &plan, cudaStream_t stream);
 cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &plan, cudaStream_t stream);

@@ -191,7 +191,7 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
         return launch_xwait(s, st);
     };
     auto carries = [&](int rows, int cols, int fmt, int epi) {
-        return xf && gemv_rows_takes(rows, cols, fmt, epi, s->ctx->sm_count, s->ctx->smem_optin);
+        return xf && gemv_fused_takes(rows, cols, fmt, epi, s->ctx->sm_count, s->ctx->smem_optin);
     };
     TRYCUDA(launch_embed(s->embd.payload, H, s->d_token, s->d_pos, s->d_tokens, s->d_hidden, s->d_rope, s->rope_base,
                          hd, st, pdl),
@@ -392,12 +392,12 @@ static int session_upload(satori_session *s, const satori_model_desc *d)
             if (L.q_bias)
                 TRY(stack_vectors(s, {{&L.q_bias, s->q_local}, {&L.k_bias, s->kv_local}, {&L.v_bias, s->kv_local}},
                                   &L.qkv_bias));
-            L.qkv_norm = gemv_rows_takes(L.qkv.rows, H, L.qkv.format, L.qkv_bias ? kEpiBias : kEpiNone,
+            L.qkv_norm = gemv_fused_takes(L.qkv.rows, H, L.qkv.format, L.qkv_bias ? kEpiBias : kEpiNone,
                                          s->ctx->sm_count, s->ctx->smem_optin);
         }
         const int nf = s->f1 - s->f0;
         if (s->fuse && L.gate.format == L.up.format &&
-            gemv_rows_takes(2 * nf, H, L.gate.format, kEpiSwiGlu, s->ctx->sm_count, s->ctx->smem_optin))
+            gemv_fused_takes(2 * nf, H, L.gate.format, kEpiSwiGlu, s->ctx->sm_count, s->ctx->smem_optin))
             TRY(combine_rows(s, {&L.gate, &L.up}, true, &L.gu));
     }
     const satori_tensor *e = find_tensor(d, "token_embd.weight");

@@ -125,6 +125,26 @@ def test_decode_order_row_widths_bit_exact(sat, ctx, oracle_lib, fmt, rows, cols
                   "batch")
 
 
+@pytest.mark.parametrize("cols", [1536, 3584, 4096, 8960, 18944])
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_fixed_width_stream_kernel_bit_exact(sat, ctx, oracle_lib, fmt, cols):
+    """The decode configurations' row widths take gemv_stream (width fixed at compile time): one row,
+    a row count that leaves partial stages and fold batches, and one that spans every CTA."""
+    bb = 34 if fmt == 0 else 18
+    for rows in (1, 37, 1003):
+        rng = np.random.default_rng(rows * 7 + cols + fmt)
+        payload = rng.integers(0, 256, size=rows * (cols // 32) * bb, dtype=np.uint8)
+        scales = (rng.standard_normal(rows * (cols // 32)) * 0.05).astype(np.float16).view(np.uint16)
+        p2 = payload.reshape(-1, bb)
+        p2[:, 0] = scales & 0xFF
+        p2[:, 1] = scales >> 8
+        x = rng.standard_normal(cols).astype(np.float32)
+        m = sat.CudaMatrixFactory(ctx).create(payload, sat.QuantizedMatrixShape(rows, cols, fmt))
+        _assert_exact(m.execute_batch(x, 1),
+                      oracle_lib.q_matvec(payload, rows, cols, fmt, x, order="batch", threads=8), ("batch", rows))
+        m.dispose()
+
+
 @pytest.mark.parametrize("positions", [2, 3, 8, 11])
 def test_batch_positions_bit_exact(sat, ctx, oracle_lib, positions):
     """ExecuteBatch with several positions: each position's rows equal the reference's."""
