@@ -109,7 +109,7 @@ __device__ __forceinline__ void st_compute(const StreamArgs &a, uint8_t *smem, i
     const int set = cw / G::WPR;
     const int e = (cw % G::WPP) * 32 + lane;                 // column within the phase
     const bool valid = e < G::HALF;
-    const int b = 2 * min(e, G::HALF - 1) + PH;              // block index in the row
+    const int b = 2 * min(e, G::HALF - 1) + (PH ? 1 : 0);    // block index in the row (odd blocks: PH = 2)
     float4 xv[8];
     {
         const double scale = a.norm_w ? rms_scale(h.red, NB * 32, a.norm_eps) : 0.0;
