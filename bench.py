@@ -12,7 +12,7 @@ split by rows, attention by query heads, vectors all-gathered over NVLink inside
 strong scaling, value = tokens / max-over-ranks device time.
 
 Before timing, at every N, a short parity check runs the session on the same 7B tensors for 4 prompt
-tokens + 4 greedy tokens and compares every step's logits (1e-4 relative + 1e-5 absolute) and greedy
+tokens + 4 greedy tokens and compares every step's logits (1e-4 relative + 5e-5 absolute) and greedy
 token (identical) with the CPU oracle's DenseSession restatement; the line carries the result.
 
 At N = 1 the line also carries `kernels` (each hot kernel alone, >= 5 repeats of >= 0.5 s regions,
@@ -43,7 +43,7 @@ sys.path.insert(0, ROOT)
 import numpy as np  # noqa: E402
 
 GB = 1e9
-LOGIT_REL, LOGIT_ABS = 1e-4, 1e-5      # stated tolerance on logits after a full decode step
+LOGIT_REL, LOGIT_ABS = 1e-4, 5e-5      # stated tolerance on logits after a full decode step (as the tests)
 
 
 def _peaks():

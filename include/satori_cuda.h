@@ -42,6 +42,8 @@ typedef enum satori_status {
 typedef enum satori_format {
     SATORI_Q8_0 = 0,
     SATORI_Q4_0 = 1,
+    SATORI_Q4_K = 12,   /* GGUF Q4_K: 256-weight super-blocks of 144 bytes (Q4KCodec.cs) */
+    SATORI_Q6_K = 14,   /* GGUF Q6_K: 256-weight super-blocks of 210 bytes (Q6KCodec.cs) */
     SATORI_T2_64 = 64,
     SATORI_T2_128 = 128,
     SATORI_T2_256 = 256
@@ -223,6 +225,46 @@ SATORI_API int satori_session_info(const satori_session *s, int *kernels_per_ste
  * 1 = final_norm output, 2 = logits (stage parity, ForwardObserver in DenseForward.cs:6). */
 SATORI_API int satori_session_stage(const satori_session *s, int which, float *out, size_t n);
 SATORI_API int satori_session_destroy(satori_session *s);  /* idempotent like DenseSession.Dispose */
+
+/* ------------------------------------------------------------------ GGUF / STQ2 files */
+typedef struct satori_gguf satori_gguf;
+/* GgufFile(path) (src/Satori.Formats.Gguf/GgufFile.cs:18-176): maps the file read-only and validates
+ * the GGUF v3 catalogue with the reference's rules; InvalidDataException -> SATORI_ERR_INVALID_DATA,
+ * NotSupportedException -> SATORI_ERR_NOT_SUPPORTED.  Host code only (no GPU needed). */
+SATORI_API int satori_gguf_open(const char *path, satori_gguf **out);
+SATORI_API int satori_gguf_close(satori_gguf *g);
+/* GgufFile.Tensors.Count / Metadata.Count. */
+SATORI_API int satori_gguf_counts(const satori_gguf *g, int *tensors, int *metadata);
+/* GgufTensor (GgufTensor.cs): name, GGUF type id, rank, dims (dims[0] = row length; unused dims 1),
+ * absolute file offset and byte length of the payload. */
+SATORI_API int satori_gguf_tensor_info(const satori_gguf *g, int index, char *name, size_t name_cap, int *type,
+                                       int *rank, int64_t *dims, int64_t *offset, int64_t *bytes);
+/* Index of a tensor by name, -1 when absent. */
+SATORI_API int satori_gguf_find_tensor(const satori_gguf *g, const char *name, int *index);
+/* GgufFile.ReadTensor (GgufFile.cs:42-49): the payload inside the mapping (valid until close). */
+SATORI_API const void *satori_gguf_tensor_data(const satori_gguf *g, int index);
+/* GgufMetadata (GgufMetadata.cs): key, value type, element type and count of entry `index` (arrays:
+ * type 9; scalars: elem_type -1, count 1). */
+SATORI_API int satori_gguf_metadata(const satori_gguf *g, int index, char *key, size_t key_cap, int *type,
+                                    int *elem_type, int64_t *count);
+/* GgufFile.ReadScalar (GgufFile.cs:56-76): the scalar's little-endian bytes (strings: their UTF-8 bytes,
+ * no terminator) into out[cap]; *written = the value's byte length.  Arrays are refused. */
+SATORI_API int satori_gguf_read_scalar(const satori_gguf *g, const char *key, int *type, void *out, size_t cap,
+                                       size_t *written);
+/* GgufModelLoader.Load + DenseTransformerAdapter.Validate (src/Satori.Core/Model/DenseTransformerAdapter.cs:
+ * 12-121): the model description of a qwen2 / qwen3 file, with `tensors[capacity]` filled with the tensors a
+ * session reads (host pointers into the mapping).  *needed = the entries required (call with capacity 0 to
+ * size the table). */
+SATORI_API int satori_gguf_model_desc(const satori_gguf *g, satori_model_desc *desc, satori_tensor *tensors,
+                                      int capacity, int *needed);
+/* DenseSession over a GGUF file: satori_gguf_model_desc then satori_session_create, every tensor uploaded
+ * once from the mapping, unchanged in layout. */
+SATORI_API int satori_session_create_from_gguf(satori_ctx *ctx, const satori_gguf *g, int context,
+                                               satori_session **out);
+/* MappedTernary2Matrix(path) (src/Satori.Core/MappedTernary2Matrix.cs:9-30) with Ternary2FileFormat.ReadHeader
+ * (Ternary2FileFormat.cs:21-35): an STQ2 file mapped, its header, length and payload validated
+ * (SATORI_ERR_INVALID_DATA on any defect), the payload uploaded once. */
+SATORI_API int satori_stq2_open(satori_ctx *ctx, const char *path, satori_matrix **out);
 
 #ifdef __cplusplus
 }

@@ -9,6 +9,7 @@ from ._lib import (ArgumentError, ContextFullError, DeviceError, DisposedError, 
 from .core import (AttentionCache, BlockQuantization, Context, CudaMatrixFactory, CudaQuantizedMatrix,
                    MappedTernary2Matrix, QuantizedMatrixShape, Ternary2Matrix, Ternary2MatVec, TransformerOps,
                    default_context, stq2_header, stq2_read_header, ternary2_byte_length)
+from .gguf import GgufFile, GgufMetadata, GgufTensor, open_stq2, session_from_gguf
 from .model import (CudaDenseSession, ModelSpec, broadcast_nccl_id, nccl_unique_id, qwen2_1_5b, qwen2_7b,
                     shard_ranges, tiny)
 
@@ -19,4 +20,5 @@ __all__ = [
     "MappedTernary2Matrix", "QuantizedMatrixShape", "Ternary2Matrix", "Ternary2MatVec", "TransformerOps",
     "default_context", "stq2_header", "stq2_read_header", "ternary2_byte_length", "CudaDenseSession", "ModelSpec",
     "qwen2_1_5b", "qwen2_7b", "tiny", "nccl_unique_id", "broadcast_nccl_id", "shard_ranges",
+    "GgufFile", "GgufMetadata", "GgufTensor", "open_stq2", "session_from_gguf",
 ]

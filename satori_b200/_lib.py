@@ -123,6 +123,18 @@ _SIGS = {
     "satori_session_info": (C.c_int, [_vp, _i32p, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
     "satori_session_stage": (C.c_int, [_vp, C.c_int, _vp, C.c_size_t]),
     "satori_session_destroy": (C.c_int, [_vp]),
+    "satori_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(_vp)]),
+    "satori_gguf_close": (C.c_int, [_vp]),
+    "satori_gguf_counts": (C.c_int, [_vp, _i32p, _i32p]),
+    "satori_gguf_tensor_info": (C.c_int, [_vp, C.c_int, C.c_char_p, C.c_size_t, _i32p, _i32p,
+                                          C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    "satori_gguf_find_tensor": (C.c_int, [_vp, C.c_char_p, _i32p]),
+    "satori_gguf_tensor_data": (_vp, [_vp, C.c_int]),
+    "satori_gguf_metadata": (C.c_int, [_vp, C.c_int, C.c_char_p, C.c_size_t, _i32p, _i32p, C.POINTER(C.c_int64)]),
+    "satori_gguf_read_scalar": (C.c_int, [_vp, C.c_char_p, _i32p, _vp, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "satori_gguf_model_desc": (C.c_int, [_vp, C.POINTER(ModelDesc), _vp, C.c_int, _i32p]),
+    "satori_session_create_from_gguf": (C.c_int, [_vp, _vp, C.c_int, C.POINTER(_vp)]),
+    "satori_stq2_open": (C.c_int, [_vp, C.c_char_p, C.POINTER(_vp)]),
 }
 
 EXPORTED = tuple(_SIGS)

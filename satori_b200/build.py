@@ -37,7 +37,7 @@ def _nvcc() -> str:
 
 
 def sources():
-    return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
 
 
 def _inputs():
@@ -53,7 +53,7 @@ def stale() -> bool:
 
 
 def _compile(src: str, extra, verbose: bool) -> str:
-    obj = os.path.join(BUILD_DIR, os.path.basename(src)[:-3] + ".o")
+    obj = os.path.join(BUILD_DIR, os.path.splitext(os.path.basename(src))[0] + ".o")
     cmd = [_nvcc(), *NVCC_FLAGS, *extra, "-c", "-o", obj, src]
     if verbose:
         print(" ".join(cmd), flush=True)

@@ -167,6 +167,18 @@ class CudaQuantizedMatrix:
         m.rows, m.columns, m.format = rows, columns, fmt
         return m
 
+    @classmethod
+    def _adopt(cls, ctx: Context, handle):
+        """Wraps a matrix handle created by a native loader (satori_stq2_open)."""
+        m = cls.__new__(cls)
+        m.ctx = ctx
+        m._h = handle
+        rows, cols, fmt, nbytes = C.c_int(), C.c_int(), C.c_int(), C.c_size_t()
+        check(_lib.lib().satori_matrix_info(handle, C.byref(rows), C.byref(cols), C.byref(fmt), C.byref(nbytes)),
+              "info")
+        m.rows, m.columns, m.format = rows.value, cols.value, fmt.value
+        return m
+
     @property
     def handle(self):
         if not self._h:

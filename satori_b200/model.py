@@ -205,6 +205,20 @@ class CudaDenseSession:
         self.context_length = context_length
         self.vocab = spec.vocab
 
+    @classmethod
+    def _adopt(cls, handle, ctx: Context, context_length: int, shape: dict):
+        """Wraps a session handle created by a native loader (satori_session_create_from_gguf)."""
+        s = cls.__new__(cls)
+        s.ctx = ctx
+        s._h = handle
+        s.context_length = context_length
+        s.vocab = shape["vocab"]
+        s.spec = ModelSpec(layers=shape["layers"], hidden=shape["hidden"], ffn=shape["ffn"],
+                           q_heads=shape["q_heads"], kv_heads=shape["kv_heads"], head_dim=shape["head_dim"],
+                           vocab=shape["vocab"], eps=shape["rms_epsilon"], rope_base=shape["rope_base"],
+                           tied_embeddings=shape["tied_embeddings"], name="gguf")
+        return s
+
     @property
     def handle(self):
         if not self._h:

@@ -48,6 +48,18 @@ def main(ref: str) -> None:
             "decoded_weights": entry["decoded_weights"], "ones_dot_product": entry["ones_dot_product"],
         }
 
+    # The whole fixture files (160-224 bytes each), for the native GGUF reader's tests.
+    gguf_files = {}
+    for entry in manifest["fixtures"]:
+        raw = open(os.path.join(gguf_dir, entry["file"]), "rb").read()
+        gguf_files[entry["file"]] = {
+            "hex": raw.hex(), "sha256": entry["sha256"], "tensor_name": entry["tensor_name"],
+            "tensor_type_id": entry["tensor_type_id"], "dimensions": entry["dimensions"],
+            "data_start": entry["data_start"], "payload_bytes": entry["payload_bytes"],
+            "alignment": entry["alignment"], "metadata_count": entry["metadata_count"],
+            "decoded_weights": entry["decoded_weights"],
+        }
+
     ops = os.path.join(ref, "fixtures", "operators")
     v1 = json.load(open(os.path.join(ops, "transformer-v1.json")))
     v2 = json.load(open(os.path.join(ops, "transformer-v2.json")))
@@ -62,6 +74,7 @@ def main(ref: str) -> None:
         "generated_from": "Satori reference fixtures; regenerate with tests/golden/make_golden.py",
         "tolerance_operator": {"abs": 2e-6, "rel": 2e-6, "stated_in": "QwenOperatorTests.cs:24; TransformerOpsTests.cs:16"},
         "gguf_v1": gguf,
+        "gguf_v1_files": {"source": "fixtures/gguf/v1/*.gguf and manifest.json", "files": gguf_files},
         "transformer_v1": v1,
         "transformer_v2": v2,
         "attention_boundaries_v1": {"source": "fixtures/operators/attention-boundaries-v1.json",

@@ -1,0 +1,205 @@
+"""The native GGUF v3 reader (satori_gguf_open, host code: no GPU) against the reference's own GGUF
+fixtures and its structure tests (tests/Satori.Numerics.Tests/GgufTests.cs, GgufStructureTests.cs).
+
+InvalidDataException maps to InvalidDataError, NotSupportedException to NotSupportedError."""
+import math
+import struct
+
+import numpy as np
+import pytest
+
+import gguf_util as G
+from golden_util import golden
+
+
+@pytest.fixture(scope="module")
+def sat():
+    from satori_b200 import build
+    build.build()
+    import satori_b200
+    return satori_b200
+
+
+def _file(tmp_path, data: bytes, name="t.gguf"):
+    p = tmp_path / name
+    p.write_bytes(data)
+    return str(p)
+
+
+FILES = golden()["gguf_v1_files"]["files"]
+
+
+@pytest.mark.parametrize("name,type_id,length,offset", [("q4_0", 2, 18, 160), ("q8_0", 8, 34, 160),
+                                                        ("f32", 0, 12, 128), ("f16", 1, 6, 128)])
+def test_golden_catalogue(sat, oracle_lib, tmp_path, name, type_id, length, offset):
+    """GgufTests.GoldenCatalogueAndScopedBounds (GgufTests.cs:31-47) and the fixture manifest."""
+    f = FILES[name + ".gguf"]
+    with sat.GgufFile(_file(tmp_path, bytes.fromhex(f["hex"]))) as g:
+        assert list(g.tensors) == [f["tensor_name"]] == ["weights"]
+        t = g.tensors["weights"]
+        assert (t.type, t.byte_length, t.offset) == (type_id, length, offset)
+        assert list(t.dimensions) == f["dimensions"]
+        assert len(g.metadata) == f["metadata_count"]
+        assert g.read_scalar("general.architecture") == "llama"
+        payload = g.read_tensor("weights")
+        assert payload.size == f["payload_bytes"]
+        if type_id in (2, 8):
+            assert g.read_scalar("general.quantization_version") == 2
+            decoded = oracle_lib.q_decode_row(payload, t.dimensions[0], 0 if type_id == 8 else 1)
+        else:
+            decoded = payload.view(np.float32 if type_id == 0 else np.float16).astype(np.float32)
+        assert decoded.tolist() == f["decoded_weights"]
+
+
+def test_every_truncation_rejects(sat, tmp_path):
+    """GgufTests.EveryTruncationRejectsWithoutPublishingCatalogue (GgufTests.cs:49-58)."""
+    raw = bytes.fromhex(FILES["q8_0.gguf"]["hex"])
+    for n in range(len(raw)):
+        with pytest.raises(sat.InvalidDataError):
+            sat.GgufFile(_file(tmp_path, raw[:n], f"t{n}.gguf"))
+
+
+def test_mutations_and_unsupported_version(sat, tmp_path):
+    """GgufTests.MutatedStructureAndUnsupportedVersionReject (GgufTests.cs:60-74)."""
+    raw = bytes.fromhex(FILES["q8_0.gguf"]["hex"])
+    for index in (0, 32, 45, 137):
+        b = bytearray(raw)
+        b[index] = 0xFF
+        with pytest.raises(sat.InvalidDataError):
+            sat.GgufFile(_file(tmp_path, bytes(b), f"m{index}.gguf"))
+    b = bytearray(raw)
+    b[4:8] = struct.pack("<I", 2)
+    with pytest.raises(sat.NotSupportedError):
+        sat.GgufFile(_file(tmp_path, bytes(b), "v2.gguf"))
+
+
+def test_repeated_reads_are_stable(sat, tmp_path):
+    """GgufTests.RepeatedMappedStringReadsKeepNamesAndScalarTypesStable (GgufTests.cs:8-19)."""
+    path = _file(tmp_path, bytes.fromhex(FILES["q8_0.gguf"]["hex"]))
+    for _ in range(200):
+        with sat.GgufFile(path) as g:
+            assert g.read_scalar("general.architecture") == "llama"
+            assert g.read_scalar("general.quantization_version") == 2
+            assert g.tensors["weights"].type == 8
+
+
+def test_closed_file_refuses_access(sat, tmp_path):
+    g = sat.GgufFile(_file(tmp_path, bytes.fromhex(FILES["q8_0.gguf"]["hex"])))
+    g.close()
+    with pytest.raises(sat.DisposedError):
+        g.read_scalar("general.architecture")
+
+
+def _scalar_value(t):
+    return {0: 17, 1: -17, 2: 17, 3: -17, 4: 17, 5: -17, 6: float("inf"), 7: 1, 8: "è\0漢", 9: (G.BOOL, [0, 1]),
+            10: 17, 11: -17, 12: float("nan")}[t]
+
+
+@pytest.mark.parametrize("alignment", [8, 64, 4096])
+def test_mixed_scalar_types_and_flat_arrays(sat, tmp_path, alignment):
+    """GgufStructureTests.MixedTensorsAllScalarTypesAndFlatArrays (GgufStructureTests.cs:7-35)."""
+    meta = b"".join(G.entry(f"custom.value_{t}", t, _scalar_value(t)) for t in range(13))
+    meta += G.entry("custom.empty", G.ARR, (G.STR, []))
+    meta += G.entry("custom.strings", G.ARR, (G.STR, ["è\0漢", ""]))
+    pre = G.prefix(alignment, meta, 15)
+    with sat.GgufFile(_file(tmp_path, G.file_with(pre, len(pre) + alignment * 2 + 3))) as g:
+        assert len(g.tensors) == 2 and len(g.metadata) == 17
+        assert g.read_scalar("custom.value_8") == "è\0漢"
+        assert g.read_scalar("custom.value_4") == 17
+        assert g.read_scalar("custom.value_11") == -17
+        assert g.read_scalar("custom.value_6") == math.inf
+        assert math.isnan(g.read_scalar("custom.value_12"))
+        assert g.read_scalar("custom.value_7") is True
+        assert g.metadata["custom.empty"].element_count == 0
+        assert g.metadata["custom.strings"].element_count == 2
+        assert g.tensors["second"].offset == len(pre) + alignment
+        with pytest.raises(sat.ArgumentError):
+            g.read_scalar("custom.strings")
+
+
+@pytest.mark.parametrize("split_count,split_no,rejected", [(0, 0, False), (1, 0, False), (2, 0, True), (1, 1, True)])
+def test_split_count(sat, tmp_path, split_count, split_no, rejected):
+    """GgufStructureTests.SplitCountZeroIsTreatedAsUnsharded (GgufStructureTests.cs:65-82)."""
+    meta = G.entry("split.count", G.U16, split_count) + G.entry("split.no", G.U16, split_no)
+    pre = G.prefix(32, meta, 2)
+    path = _file(tmp_path, G.file_with(pre, len(pre) + 64))
+    if rejected:
+        with pytest.raises(sat.NotSupportedError):
+            sat.GgufFile(path)
+    else:
+        with sat.GgufFile(path) as g:
+            assert len(g.tensors) == 2
+
+
+@pytest.mark.parametrize("defect", ["bool", "key", "duplicate", "utf8", "typed"])
+def test_invalid_metadata_rejects(sat, tmp_path, defect):
+    """GgufStructureTests.InvalidMetadataRejects (GgufStructureTests.cs:100-118)."""
+    key = {"key": "BAD.key", "duplicate": "general.architecture", "typed": "general.file_type"}.get(defect, "custom.test")
+    meta = G.gstr(key)
+    if defect == "utf8":
+        meta += struct.pack("<IQ", 8, 1) + b"\xff"
+    else:
+        meta += struct.pack("<I", 7) + bytes([2 if defect == "bool" else 1])
+    pre = G.prefix(32, meta, 1)
+    with pytest.raises(sat.InvalidDataError):
+        sat.GgufFile(_file(tmp_path, G.file_with(pre, len(pre) + 64)))
+
+
+@pytest.mark.parametrize("defect", ["overlap", "overflow", "zero", "unaligned", "duplicate"])
+def test_invalid_tensor_structure_rejects(sat, tmp_path, defect):
+    """GgufStructureTests.InvalidTensorStructureRejects (GgufStructureTests.cs:120-139)."""
+    tensors = {"overlap": [("a", [32], 0, 0), ("b", [1], 0, 32)],
+               "overflow": [("a", [2 ** 63 - 1, 2], 0, 0)],
+               "zero": [("a", [0], 0, 0)],
+               "unaligned": [("a", [1], 0, 1)],
+               "duplicate": [("a", [1], 0, 0), ("a", [1], 0, 32)]}[defect]
+    pre = G.prefix(32, tensors=tensors)
+    with pytest.raises(sat.InvalidDataError):
+        sat.GgufFile(_file(tmp_path, G.file_with(pre, len(pre) + 256)))
+
+
+def test_gap_and_reverse_order_are_unsupported(sat, tmp_path):
+    """GgufStructureTests.GapAndReversePhysicalOrderAreUnsupportedRatherThanCorrupt (:141-152)."""
+    for offsets in ((32, 64), (32, 0)):
+        pre = G.prefix(32, tensors=[("a", [1], 0, offsets[0]), ("b", [1], 0, offsets[1])])
+        with pytest.raises(sat.NotSupportedError):
+            sat.GgufFile(_file(tmp_path, G.file_with(pre, len(pre) + 128)))
+
+
+def test_k_quant_types_are_accepted(sat, tmp_path):
+    """GgufStructureTests.KQuantizedTypesAreAcceptedByTheExtendedProfile (:154-170)."""
+    meta = G.entry("general.quantization_version", G.U32, 2)
+    pre = G.prefix(32, meta, 1, [("q4k", [256, 2], 12, 0), ("q6k", [256, 1], 14, 288)])
+    with sat.GgufFile(_file(tmp_path, G.file_with(pre, len(pre) + 512))) as g:
+        assert (g.tensors["q4k"].type, g.tensors["q6k"].type) == (12, 14)
+        assert (g.tensors["q4k"].byte_length, g.tensors["q6k"].byte_length) == (288, 210)
+
+
+def test_missing_quantization_version_and_unsupported_type(sat, tmp_path):
+    pre = G.prefix(32, tensors=[("q", [32], 8, 0)])
+    with pytest.raises(sat.InvalidDataError):
+        sat.GgufFile(_file(tmp_path, G.file_with(pre, len(pre) + 64)))
+    pre = G.prefix(32, G.entry("general.quantization_version", G.U32, 2), 1, [("q", [32], 3, 0)])
+    with pytest.raises(sat.NotSupportedError):
+        sat.GgufFile(_file(tmp_path, G.file_with(pre, len(pre) + 64)))
+
+
+def test_model_description_from_metadata(sat, tmp_path):
+    """DenseTransformerAdapter.Validate over a qwen2 container: shape from {arch}.* keys, vocabulary from
+    token_embd.weight, untied output, optional biases; a missing tensor is a capability gap."""
+    from model_util import synthetic_tensors
+    spec = sat.tiny()
+    tensors = synthetic_tensors(spec, 3)
+    data = G.model_gguf(spec, tensors)
+    with sat.GgufFile(_file(tmp_path, data)) as g:
+        d = g.model_desc()
+        assert (d["layers"], d["hidden"], d["ffn"], d["q_heads"], d["kv_heads"], d["head_dim"], d["vocab"]) == \
+            (spec.layers, spec.hidden, spec.ffn, spec.q_heads, spec.kv_heads, spec.head_dim, spec.vocab)
+        assert d["rope_base"] == spec.rope_base and not d["tied_embeddings"]
+        assert d["tensors"] == len(tensors)
+        assert np.array_equal(g.read_tensor("blk.1.ffn_down.weight"), tensors["blk.1.ffn_down.weight"])
+    broken = dict(tensors)
+    del broken["blk.0.attn_k.weight"]
+    with sat.GgufFile(_file(tmp_path, G.model_gguf(spec, broken), "broken.gguf")) as g:
+        with pytest.raises(sat.NotSupportedError):
+            g.model_desc()

@@ -228,6 +228,33 @@ def test_ternary2_import_rejections(sat, ctx):
             sat.Ternary2Matrix.from_packed(1, 1, 64, p, ctx=ctx)
 
 
+def test_native_stq2_reader_equals_owned_and_rejects_corruption(sat, ctx, tmp_path):
+    """satori_stq2_open (MappedTernary2Matrix in native code): equal to the owned matrix bitwise, and the
+    header / length / payload corruptions of MappedTernary2Tests.cs:32-69 raise InvalidDataError."""
+    name, rows, cols, w, x = numerical_random(7, 257)
+    owned = sat.Ternary2Matrix.quantize(w, rows, cols, 64, ctx=ctx)
+    path = str(tmp_path / "m.stq2")
+    owned.save(path)
+    m = sat.open_stq2(path, ctx=ctx)
+    assert (m.rows, m.columns, m.format) == (rows, cols, 64)
+    assert bits_equal(m.execute(x), sat.Ternary2MatVec.execute(owned, x))
+    m.dispose()
+    one = sat.Ternary2Matrix.quantize(np.array([1.0], np.float32), 1, 1, 64, ctx=ctx)
+    p1 = str(tmp_path / "one.stq2")
+    one.save(p1)
+    original = open(p1, "rb").read()
+    corruptions = [original[:10], original[:-1], original + b"\x00"]
+    for index in (0, 4, 6, 8, 16, 20, 24):
+        c = bytearray(original)
+        c[index] ^= 0xFF
+        corruptions.append(bytes(c))
+    for i, data in enumerate(corruptions):
+        pc = str(tmp_path / f"n{i}.stq2")
+        open(pc, "wb").write(data)
+        with pytest.raises(sat.InvalidDataError):
+            sat.open_stq2(pc, ctx=ctx)
+
+
 def test_mapped_ternary2_equals_owned_and_rejects_corruption(sat, ctx, tmp_path):
     """MappedTernary2Tests.cs:9-30 (mapped == owned, bitwise), :32-69 (12 corruptions) and :71-89."""
     name, rows, cols, w, x = numerical_random(7, 257)
