@@ -193,6 +193,62 @@ def q_quantize(w: np.ndarray, rows: int, cols: int, fmt: int) -> np.ndarray:
     return out
 
 
+# ---------------------------------------------------------------- K-quants (Q4_K, Q6_K; Q8_K activations)
+Q4_K, Q6_K = 12, 14
+
+
+def k_geometry(rows: int, cols: int, fmt: int):
+    bb, ln = C.c_int(), C.c_int64()
+    _check(lib().so_k_geometry(rows, cols, fmt, C.byref(bb), C.byref(ln)), "k_geometry")
+    return bb.value, ln.value
+
+
+def k_validate(data, rows: int, cols: int, fmt: int) -> int:
+    d = _c_u8(data)
+    return lib().so_k_validate(_u8(d), C.c_int64(d.size), rows, cols, fmt)
+
+
+def k_decode_row(row_bytes, cols: int, fmt: int) -> np.ndarray:
+    d = _c_u8(row_bytes)
+    out = np.zeros(cols, dtype=np.float32)
+    _check(lib().so_k_decode_row(_u8(d), cols, fmt, _f32(out)), "k_decode_row")
+    return out
+
+
+def k_matvec(data, rows: int, cols: int, fmt: int, x, order: str = "batch", positions: int = 1,
+             threads: int = 1) -> np.ndarray:
+    d, xv = _c_u8(data), _c_f32(x)
+    L = lib()
+    if order == "batch":
+        y = np.zeros(rows * positions, dtype=np.float32)
+        rc = L.so_k_matvec_batch(_u8(d), rows, cols, fmt, _f32(xv), positions, _f32(y), threads)
+    elif order == "avx2":
+        y = np.zeros(rows, dtype=np.float32)
+        rc = L.so_k_matvec_avx2(_u8(d), rows, cols, fmt, _f32(xv), _f32(y), threads)
+    elif order == "scalar":
+        y = np.zeros(rows, dtype=np.float32)
+        rc = L.so_k_matvec_scalar(_u8(d), rows, cols, fmt, _f32(xv), _f32(y))
+    else:
+        raise ValueError(order)
+    _check(rc, "k_matvec")
+    return y
+
+
+def q8k_quantize_row(x) -> np.ndarray:
+    xv = _c_f32(x)
+    out = np.zeros(xv.size // 256 * 292, dtype=np.uint8)
+    _check(lib().so_q8k_quantize_row(_f32(xv), xv.size, _u8(out)), "q8k_quantize_row")
+    return out
+
+
+def k_int_dot(block, fmt: int, activation):
+    """(integer product, min product) of one K-quant block with one Q8_K activation block."""
+    b, a = _c_u8(block), _c_u8(activation)
+    dot, mins = C.c_int32(), C.c_int32()
+    _check(lib().so_k_int_dot(_u8(b), fmt, _u8(a), C.byref(dot), C.byref(mins)), "k_int_dot")
+    return dot.value, mins.value
+
+
 # ---------------------------------------------------------------- operators
 def rmsnorm(x, w, eps: float) -> np.ndarray:
     xv, wv = _c_f32(x), _c_f32(w)

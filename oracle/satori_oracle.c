@@ -860,3 +860,336 @@ int so_session_stage(const so_session *s, int which, float *out, int n)
     memcpy(out, src, sizeof(float) * (size_t)n);
     return SO_OK;
 }
+
+/* ------------------------------------------------------------------------- */
+/* GGUF K-quants: Q4_K / Q6_K weights, Q8_K activations                      */
+/* ------------------------------------------------------------------------- */
+
+/* QuantizedMatrixShape.cs:11-12: 256 weights per super-block; Q4_K 144 bytes, Q6_K 210. */
+int so_k_geometry(int rows, int cols, int fmt, int *block_bytes, int64_t *byte_length)
+{
+    int bb;
+    if (fmt == SO_Q4_K) bb = 144;
+    else if (fmt == SO_Q6_K) bb = 210;
+    else return SO_ERR_ARGUMENT;
+    if (rows <= 0 || cols <= 0 || cols % 256 != 0) return SO_ERR_ARGUMENT;
+    int64_t len = (int64_t)rows * (cols / 256) * bb;
+    if (len > 0x7fffffffLL) return SO_ERR_ARGUMENT;
+    if (block_bytes) *block_bytes = bb;
+    if (byte_length) *byte_length = len;
+    return SO_OK;
+}
+
+/* QuantizedMatVec.ValidatePayload (QuantizedMatVec.cs:28-42) with Q4KCodec.AreScalesFinite (d, dmin)
+ * and Q6KCodec.AreScalesFinite (d at byte 208). */
+int so_k_validate(const uint8_t *data, int64_t len, int rows, int cols, int fmt)
+{
+    int bb; int64_t want;
+    int rc = so_k_geometry(rows, cols, fmt, &bb, &want);
+    if (rc) return rc;
+    if (len != want) return SO_ERR_ARGUMENT;
+    for (int64_t off = 0; off < len; off += bb) {
+        const uint8_t *b = data + off;
+        if (fmt == SO_Q4_K) {
+            if (!isfinite_f(so_half_to_float(rd16(b))) || !isfinite_f(so_half_to_float(rd16(b + 2))))
+                return SO_ERR_INVALID_DATA;
+        } else if (!isfinite_f(so_half_to_float(rd16(b + 208)))) {
+            return SO_ERR_INVALID_DATA;
+        }
+    }
+    return SO_OK;
+}
+
+/* Q4KCodec.GetScaleMin (Q4KCodec.cs:24-37) */
+static void q4k_scale_min(int j, const uint8_t *scales, int *scale, int *min)
+{
+    if (j < 4) {
+        *scale = scales[j] & 63;
+        *min = scales[j + 4] & 63;
+    } else {
+        *scale = (scales[j + 4] & 0xF) | ((scales[j - 4] >> 6) << 4);
+        *min = (scales[j + 4] >> 4) | ((scales[j] >> 6) << 4);
+    }
+}
+
+/* Q4KCodec.DecodeBlock (Q4KCodec.cs:70-91): w = dl * q - ml, every product and difference rounded. */
+static void q4k_decode_block(const uint8_t *b, float *w)
+{
+    float d = so_half_to_float(rd16(b)), dmin = so_half_to_float(rd16(b + 2));
+    const uint8_t *scales = b + 4, *quants = b + 16;
+    for (int g = 0; g < 4; g++) {
+        const uint8_t *qs = quants + g * 32;
+        int s0, n0, s1, n1;
+        q4k_scale_min(g * 2, scales, &s0, &n0);
+        q4k_scale_min(g * 2 + 1, scales, &s1, &n1);
+        float dl = d * (float)s0, ml = dmin * (float)n0, dh = d * (float)s1, mh = dmin * (float)n1;
+        for (int l = 0; l < 32; l++) {
+            w[g * 64 + l] = dl * (float)(qs[l] & 0xF) - ml;
+            w[g * 64 + 32 + l] = dh * (float)(qs[l] >> 4) - mh;
+        }
+    }
+}
+
+/* The 6-bit code of weight (half, l, k) of a Q6_K block (Q6KCodec.cs:38-46), already centred. */
+static inline int q6k_code(const uint8_t *b, int half, int l, int k)
+{
+    const uint8_t *lql = b + half * 64, *lqh = b + 128 + half * 32;
+    int nib = k == 0 ? (lql[l] & 0xF) : k == 1 ? (lql[l + 32] & 0xF) : k == 2 ? (lql[l] >> 4) : (lql[l + 32] >> 4);
+    return (nib | (((lqh[l] >> (2 * k)) & 3) << 4)) - 32;
+}
+
+/* Q6KCodec.DecodeBlock (Q6KCodec.cs:58-85): w = d * scale * q, left to right. */
+static void q6k_decode_block(const uint8_t *b, float *w)
+{
+    float d = so_half_to_float(rd16(b + 208));
+    const int8_t *scales = (const int8_t *)(b + 192);
+    for (int half = 0; half < 2; half++)
+        for (int l = 0; l < 32; l++) {
+            int sub = l / 16;
+            for (int k = 0; k < 4; k++)
+                w[half * 128 + l + 32 * k] = d * (float)scales[half * 8 + sub + 2 * k] * (float)q6k_code(b, half, l, k);
+        }
+}
+
+int so_k_decode_row(const uint8_t *row_bytes, int cols, int fmt, float *out)
+{
+    int bb;
+    if (so_k_geometry(1, cols, fmt, &bb, NULL)) return SO_ERR_ARGUMENT;
+    for (int b = 0; b < cols / 256; b++) {
+        if (fmt == SO_Q4_K) q4k_decode_block(row_bytes + (int64_t)b * bb, out + b * 256);
+        else q6k_decode_block(row_bytes + (int64_t)b * bb, out + b * 256);
+    }
+    return SO_OK;
+}
+
+/* Q4KCodec.DotBlock (Q4KCodec.cs:40-66) */
+static float q4k_dot_block(const uint8_t *b, const float *x)
+{
+    float d = so_half_to_float(rd16(b)), dmin = so_half_to_float(rd16(b + 2));
+    const uint8_t *scales = b + 4, *quants = b + 16;
+    float total = 0;
+    for (int g = 0; g < 4; g++) {
+        const uint8_t *qs = quants + g * 32;
+        const float *low = x + g * 64, *high = x + g * 64 + 32;
+        int s0, n0, s1, n1;
+        q4k_scale_min(g * 2, scales, &s0, &n0);
+        q4k_scale_min(g * 2 + 1, scales, &s1, &n1);
+        float dl = d * (float)s0, ml = dmin * (float)n0, dh = d * (float)s1, mh = dmin * (float)n1;
+        float acc_low = 0, acc_high = 0;
+        for (int l = 0; l < 32; l++) {
+            acc_low += (dl * (float)(qs[l] & 0xF) - ml) * low[l];
+            acc_high += (dh * (float)(qs[l] >> 4) - mh) * high[l];
+        }
+        total += acc_low + acc_high;
+    }
+    return total;
+}
+
+/* Q6KCodec.DotBlock (Q6KCodec.cs:14-44) */
+static float q6k_dot_block(const uint8_t *b, const float *x)
+{
+    float d = so_half_to_float(rd16(b + 208));
+    const int8_t *scales = (const int8_t *)(b + 192);
+    float total = 0;
+    for (int half = 0; half < 2; half++)
+        for (int l = 0; l < 32; l++) {
+            int sub = l / 16;
+            for (int k = 0; k < 4; k++)
+                total += d * (float)scales[half * 8 + sub + 2 * k] * (float)q6k_code(b, half, l, k) *
+                         x[half * 128 + l + 32 * k];
+        }
+    return total;
+}
+
+/* QuantizedMatVec.ExecuteScalar for the K formats (QuantizedMatVec.cs:45-66): total += DotBlock. */
+int so_k_matvec_scalar(const uint8_t *data, int rows, int cols, int fmt, const float *x, float *y)
+{
+    int bb; int64_t len;
+    int rc = so_k_geometry(rows, cols, fmt, &bb, &len);
+    if (rc) return rc;
+    int bpr = cols / 256;
+    for (int row = 0; row < rows; row++) {
+        float total = 0;
+        for (int blk = 0; blk < bpr; blk++) {
+            const uint8_t *b = data + ((int64_t)row * bpr + blk) * bb;
+            total += fmt == SO_Q4_K ? q4k_dot_block(b, x + blk * 256) : q6k_dot_block(b, x + blk * 256);
+        }
+        y[row] = total;
+    }
+    return SO_OK;
+}
+
+/* One row of QuantizedKAvx2Kernel.ExecuteQ4K / ExecuteQ6K (QuantizedKAvx2Kernel.cs:225-331): eight float
+ * lanes per 8-weight step (multiply then add, no FMA), the fixed horizontal sum, total += it. */
+static void k_avx2_row(const uint8_t *data, int row, int cols, int fmt, int bb, const float *x, float *y)
+{
+    int bpr = cols / 256;
+    float total = 0;
+    for (int blk = 0; blk < bpr; blk++) {
+        const uint8_t *b = data + ((int64_t)row * bpr + blk) * bb;
+        const float *xb = x + blk * 256;
+        if (fmt == SO_Q4_K) {
+            float d = so_half_to_float(rd16(b)), dmin = so_half_to_float(rd16(b + 2));
+            for (int g = 0; g < 4; g++) {
+                const uint8_t *q = b + 16 + g * 32;
+                int s0, n0, s1, n1;
+                q4k_scale_min(g * 2, b + 4, &s0, &n0);
+                q4k_scale_min(g * 2 + 1, b + 4, &s1, &n1);
+                __m256 ls = _mm256_set1_ps(d * (float)s0), lb = _mm256_set1_ps(dmin * (float)n0);
+                __m256 hs = _mm256_set1_ps(d * (float)s1), hb = _mm256_set1_ps(dmin * (float)n1);
+                __m256 acc = _mm256_setzero_ps();
+                for (int j = 0; j < 32; j += 8) {
+                    uint64_t packed; memcpy(&packed, q + j, 8);
+                    __m256i codes = _mm256_cvtepu8_epi32(_mm_cvtsi64_si128((long long)packed));
+                    __m256 low = _mm256_cvtepi32_ps(_mm256_and_si256(codes, _mm256_set1_epi32(15)));
+                    __m256 high = _mm256_cvtepi32_ps(_mm256_srli_epi32(codes, 4));
+                    __m256 lw = _mm256_sub_ps(_mm256_mul_ps(low, ls), lb);
+                    __m256 hw = _mm256_sub_ps(_mm256_mul_ps(high, hs), hb);
+                    acc = _mm256_add_ps(acc, _mm256_mul_ps(lw, _mm256_loadu_ps(xb + g * 64 + j)));
+                    acc = _mm256_add_ps(acc, _mm256_mul_ps(hw, _mm256_loadu_ps(xb + g * 64 + 32 + j)));
+                }
+                total += hsum256(acc);
+            }
+        } else {
+            float d = so_half_to_float(rd16(b + 208));
+            const int8_t *scales = (const int8_t *)(b + 192);
+            for (int half = 0; half < 2; half++)
+                for (int l = 0; l < 32; l += 8) {
+                    int sub = l / 16;
+                    __m256 acc = _mm256_setzero_ps();
+                    for (int k = 0; k < 4; k++) {
+                        float c[8];
+                        for (int i = 0; i < 8; i++) c[i] = (float)q6k_code(b, half, l + i, k);
+                        __m256 w = _mm256_mul_ps(_mm256_loadu_ps(c), _mm256_set1_ps(d * (float)scales[half * 8 + sub + 2 * k]));
+                        acc = _mm256_add_ps(acc, _mm256_mul_ps(w, _mm256_loadu_ps(xb + half * 128 + l + 32 * k)));
+                    }
+                    total += hsum256(acc);
+                }
+        }
+    }
+    y[row] = total;
+}
+
+int so_k_matvec_avx2(const uint8_t *data, int rows, int cols, int fmt, const float *x, float *y, int threads)
+{
+    int bb; int64_t len;
+    int rc = so_k_geometry(rows, cols, fmt, &bb, &len);
+    if (rc) return rc;
+#pragma omp parallel for num_threads(clamp_threads(threads)) schedule(static)
+    for (int row = 0; row < rows; row++) k_avx2_row(data, row, cols, fmt, bb, x, y);
+    return SO_OK;
+}
+
+/* Q8KCodec.QuantizeBlock (Q8KCodec.cs:43-75) with NearestInteger (:104-110): 292 bytes per 256 values. */
+static void q8k_quantize_block(const float *x, uint8_t *blk)
+{
+    float max = 0, magnitude = 0;
+    for (int j = 0; j < 256; j++) {
+        float a = fabsf(x[j]);
+        if (a > magnitude) { magnitude = a; max = x[j]; }
+    }
+    if (magnitude == 0) { memset(blk, 0, 292); return; }
+    float inverse = -127.0f / max;
+    int8_t *codes = (int8_t *)(blk + 4);
+    for (int j = 0; j < 256; j++) {
+        float shifted = inverse * x[j] + 12582912.0f;
+        int v = (int)(f2u(shifted) & 0x007fffffu) - 0x00400000;
+        codes[j] = (int8_t)(v < 127 ? v : 127);
+    }
+    for (int g = 0; g < 16; g++) {
+        int total = 0;
+        for (int j = 0; j < 16; j++) total += codes[g * 16 + j];
+        int16_t s = (int16_t)total;
+        memcpy(blk + 260 + 2 * g, &s, 2);
+    }
+    float scale = 1.0f / inverse;
+    memcpy(blk, &scale, 4);
+}
+
+int so_q8k_quantize_row(const float *x, int cols, uint8_t *out)
+{
+    if (cols <= 0 || cols % 256 != 0) return SO_ERR_ARGUMENT;
+    for (int b = 0; b < cols / 256; b++) q8k_quantize_block(x + b * 256, out + (int64_t)b * 292);
+    return SO_OK;
+}
+
+/* Q4KCodec.DotProduct / MinProduct (Q4KCodec.cs:112-153) and Q6KCodec.DotProduct (Q6KCodec.cs:103-146):
+ * exact integers.  For Q4_K *min_total receives MinProduct. */
+int so_k_int_dot(const uint8_t *b, int fmt, const uint8_t *act, int32_t *dot, int32_t *min_total)
+{
+    const int8_t *codes = (const int8_t *)(act + 4);
+    int16_t sums[16];
+    memcpy(sums, act + 260, 32);
+    int total = 0, mins = 0;
+    if (fmt == SO_Q4_K) {
+        for (int g = 0; g < 4; g++) {
+            const uint8_t *qs = b + 16 + g * 32;
+            int ls, lm, hs, hm;
+            q4k_scale_min(g * 2, b + 4, &ls, &lm);
+            q4k_scale_min(g * 2 + 1, b + 4, &hs, &hm);
+            int low = 0, high = 0;
+            for (int l = 0; l < 32; l++) {
+                low += (qs[l] & 0xF) * codes[g * 64 + l];
+                high += (qs[l] >> 4) * codes[g * 64 + 32 + l];
+            }
+            total += ls * low + hs * high;
+            mins += lm * (sums[g * 4] + sums[g * 4 + 1]) + hm * (sums[g * 4 + 2] + sums[g * 4 + 3]);
+        }
+    } else if (fmt == SO_Q6_K) {
+        const int8_t *scales = (const int8_t *)(b + 192);
+        for (int half = 0; half < 2; half++)
+            for (int l = 0; l < 32; l++) {
+                int sub = l / 16;
+                for (int k = 0; k < 4; k++)
+                    total += scales[half * 8 + sub + 2 * k] * q6k_code(b, half, l, k) * codes[half * 128 + l + 32 * k];
+            }
+    } else {
+        return SO_ERR_ARGUMENT;
+    }
+    if (dot) *dot = total;
+    if (min_total) *min_total = mins;
+    return SO_OK;
+}
+
+/* QuantizedMatVec.ExecuteBatchQuantized -> QuantizedKAvx2Kernel.ExecuteQuantizedTiled
+ * (QuantizedMatVec.cs:122-220, QuantizedKAvx2Kernel.cs:46-95): activations quantized to Q8_K once; per
+ * row and block an exact integer product, then the float combine in the reference's order, summed over
+ * blocks per position; all-zero activation blocks are skipped. */
+int so_k_matvec_batch(const uint8_t *data, int rows, int cols, int fmt, const float *x, int positions, float *y,
+                      int threads)
+{
+    int bb; int64_t len;
+    int rc = so_k_geometry(rows, cols, fmt, &bb, &len);
+    if (rc) return rc;
+    if (positions <= 0 || positions > 256) return SO_ERR_ARGUMENT;
+    int bpr = cols / 256;
+    int64_t arow = (int64_t)bpr * 292;
+    uint8_t *act = (uint8_t *)malloc((size_t)(arow * positions));
+    for (int p = 0; p < positions; p++) so_q8k_quantize_row(x + (int64_t)p * cols, cols, act + p * arow);
+#pragma omp parallel for num_threads(clamp_threads(threads)) schedule(static)
+    for (int row = 0; row < rows; row++) {
+        float acc[256];
+        for (int p = 0; p < positions; p++) acc[p] = 0;
+        for (int blk = 0; blk < bpr; blk++) {
+            const uint8_t *b = data + ((int64_t)row * bpr + blk) * bb;
+            float d = fmt == SO_Q4_K ? so_half_to_float(rd16(b)) : so_half_to_float(rd16(b + 208));
+            float dmin = fmt == SO_Q4_K ? so_half_to_float(rd16(b + 2)) : 0;
+            for (int p = 0; p < positions; p++) {
+                const uint8_t *a = act + p * arow + (int64_t)blk * 292;
+                float as = rdf32(a);
+                if (as == 0) continue;
+                int32_t dot, mins;
+                so_k_int_dot(b, fmt, a, &dot, &mins);
+                if (fmt == SO_Q4_K) {
+                    float da = d * as, ma = dmin * as;
+                    acc[p] += da * (float)dot - ma * (float)mins;
+                } else {
+                    acc[p] += as * d * (float)dot;
+                }
+            }
+        }
+        for (int p = 0; p < positions; p++) y[(int64_t)p * rows + row] = acc[p];
+    }
+    free(act);
+    return SO_OK;
+}

@@ -36,6 +36,8 @@ extern "C" {
 /* Block formats (BlockQuantization.cs:3 for Q8_0/Q4_0; Ternary2 block sizes). */
 #define SO_Q8_0 0
 #define SO_Q4_0 1
+#define SO_Q4_K 12
+#define SO_Q6_K 14
 #define SO_T2_64 64
 #define SO_T2_128 128
 #define SO_T2_256 256
@@ -67,6 +69,16 @@ int so_q_matvec_batch(const uint8_t *data, int rows, int cols, int fmt, const fl
 int so_q_matvec_batch_emulated(const uint8_t *data, int rows, int cols, int fmt, const float *x, int positions,
                                float *y);
 /* Not in the reference (it only decodes): this repository's own deterministic quantizer. */
+/* K-quants (Q4KCodec.cs, Q6KCodec.cs, Q8KCodec.cs, QuantizedKAvx2Kernel.cs) */
+int so_k_geometry(int rows, int cols, int fmt, int *block_bytes, int64_t *byte_length);
+int so_k_validate(const uint8_t *data, int64_t len, int rows, int cols, int fmt);
+int so_k_decode_row(const uint8_t *row_bytes, int cols, int fmt, float *out);
+int so_k_matvec_scalar(const uint8_t *data, int rows, int cols, int fmt, const float *x, float *y);
+int so_k_matvec_avx2(const uint8_t *data, int rows, int cols, int fmt, const float *x, float *y, int threads);
+int so_q8k_quantize_row(const float *x, int cols, uint8_t *out);
+int so_k_int_dot(const uint8_t *block, int fmt, const uint8_t *activation, int32_t *dot, int32_t *min_total);
+int so_k_matvec_batch(const uint8_t *data, int rows, int cols, int fmt, const float *x, int positions, float *y,
+                      int threads);
 int so_q_quantize(const float *w, int rows, int cols, int fmt, uint8_t *out);
 
 /* ---------------- operators (src/Satori.Core/TransformerOps.cs) ---------------- */

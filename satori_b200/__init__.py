@@ -4,7 +4,7 @@ The compute lives in ``_build/libsatori_cuda.so`` (hand-written sm_100a CUDA beh
 ``include/satori_cuda.h``); this package mirrors the reference's C# API over that ABI.
 """
 from ._lib import (ArgumentError, ContextFullError, DeviceError, DisposedError, InvalidDataError,
-                   NotSupportedError, SatoriError, ORDER_BATCH, ORDER_EXECUTE, ORDER_SCALAR, Q4_0, Q8_0,
+                   NotSupportedError, SatoriError, ORDER_BATCH, ORDER_EXECUTE, ORDER_SCALAR, Q4_0, Q8_0, Q4_K, Q6_K,
                    T2_64, T2_128, T2_256, version)
 from .core import (AttentionCache, BlockQuantization, Context, CudaMatrixFactory, CudaQuantizedMatrix,
                    MappedTernary2Matrix, QuantizedMatrixShape, Ternary2Matrix, Ternary2MatVec, TransformerOps,
@@ -15,7 +15,7 @@ from .model import (CudaDenseSession, ModelSpec, broadcast_nccl_id, nccl_unique_
 
 __all__ = [
     "ArgumentError", "ContextFullError", "DeviceError", "DisposedError", "InvalidDataError", "NotSupportedError",
-    "SatoriError", "ORDER_BATCH", "ORDER_EXECUTE", "ORDER_SCALAR", "Q4_0", "Q8_0", "T2_64", "T2_128", "T2_256",
+    "SatoriError", "ORDER_BATCH", "ORDER_EXECUTE", "ORDER_SCALAR", "Q4_0", "Q8_0", "Q4_K", "Q6_K", "T2_64", "T2_128", "T2_256",
     "version", "AttentionCache", "BlockQuantization", "Context", "CudaMatrixFactory", "CudaQuantizedMatrix",
     "MappedTernary2Matrix", "QuantizedMatrixShape", "Ternary2Matrix", "Ternary2MatVec", "TransformerOps",
     "default_context", "stq2_header", "stq2_read_header", "ternary2_byte_length", "CudaDenseSession", "ModelSpec",

@@ -108,17 +108,24 @@ def default_context(device: int = 0) -> Context:
 
 # --------------------------------------------------------------------------- shapes
 class BlockQuantization(enum.IntEnum):
-    """src/Satori.Core/BlockQuantization.cs:3 (the two formats on this path)."""
+    """src/Satori.Core/BlockQuantization.cs:3 (values are the GGUF tensor type ids of the K formats)."""
     Q8_0 = _lib.Q8_0
     Q4_0 = _lib.Q4_0
+    Q4_K = _lib.Q4_K
+    Q6_K = _lib.Q6_K
+
+
+_BLOCKS = {BlockQuantization.Q8_0: (32, 34), BlockQuantization.Q4_0: (32, 18), BlockQuantization.Q4_K: (256, 144),
+           BlockQuantization.Q6_K: (256, 210)}
 
 
 class QuantizedMatrixShape:
-    """QuantizedMatrixShape (QuantizedMatrixShape.cs:5-22): positive dims, complete 32-weight rows."""
+    """QuantizedMatrixShape (QuantizedMatrixShape.cs:5-22): positive dims, complete blocks per row (32 weights
+    for Q8_0 / Q4_0, 256 for the K super-blocks)."""
 
     def __init__(self, rows: int, columns: int, fmt: BlockQuantization):
         fmt = BlockQuantization(fmt)
-        self.block_elements, self.block_bytes = (32, 34) if fmt == BlockQuantization.Q8_0 else (32, 18)
+        self.block_elements, self.block_bytes = _BLOCKS[fmt]
         if rows <= 0 or columns <= 0 or columns % self.block_elements != 0:
             raise ArgumentError(_lib.ERR_ARGUMENT,
                                 f"Positive dimensions and complete {self.block_elements}-weight rows required.")

@@ -74,7 +74,11 @@ int check_dev_error(satori_ctx *ctx)
     return SATORI_OK;
 }
 
-bool is_valid_format(int f) { return f == SATORI_Q8_0 || f == SATORI_Q4_0 || f == 64 || f == 128 || f == 256; }
+bool is_valid_format(int f)
+{
+    return f == SATORI_Q8_0 || f == SATORI_Q4_0 || f == SATORI_Q4_K || f == SATORI_Q6_K || f == 64 || f == 128 ||
+           f == 256;
+}
 
 size_t payload_bytes(int rows, int cols, int format)
 {
@@ -91,6 +95,8 @@ int validate_shape(int rows, int cols, int format)
     if (rows <= 0 || cols <= 0) return set_error(SATORI_ERR_ARGUMENT, "dimensions must be positive");
     if (format <= 1 && cols % 32 != 0)
         return set_error(SATORI_ERR_ARGUMENT, "complete 32-weight rows required (cols=%d)", cols);
+    if (is_kquant(format) && cols % 256 != 0)
+        return set_error(SATORI_ERR_ARGUMENT, "Columns must be a positive multiple of 256 (cols=%d)", cols);
     if (payload_bytes(rows, cols, format) > 0x7fffffffull)
         return set_error(SATORI_ERR_ARGUMENT, "payload exceeds Int32 limits");
     return SATORI_OK;
@@ -153,6 +159,38 @@ int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int 
              float *dy, int positions, int epilogue, const float *bias, float *residual, cudaStream_t stream,
              int use_pdl, const float *norm_w, float norm_eps, const XPush *xp, const XWait *xw)
 {
+    // The caller's hint about the next MatVec of its sequence applies to this call only.
+    const uint8_t *hint = ctx->next_payload;
+    const size_t hint_bytes = hint ? ctx->next_bytes : 0;
+    ctx->next_payload = nullptr;
+    ctx->next_bytes = 0;
+    if (is_kquant(format)) {
+        if (norm_w || xp || xw || epilogue == kEpiSwiGlu)
+            return set_error(SATORI_ERR_NOT_SUPPORTED, "fused RmsNorm / SwiGLU / exchange are not available for K-quants");
+        if (order != SATORI_ORDER_BATCH && epilogue != kEpiNone)
+            return set_error(SATORI_ERR_NOT_SUPPORTED, "K-quant epilogues need the batch order");
+        if (cols > 32768) return set_error(SATORI_ERR_NOT_SUPPORTED, "K-quant rows wider than 32768 columns");
+        // Positions are independent in every order (one accumulator per position), so one launch each.
+        for (int p = 0; p < positions; ++p) {
+            GemvArgs a = {};
+            a.payload = d_payload;
+            a.rows = rows;
+            a.cols = cols;
+            a.format = format;
+            a.order = order;
+            a.x = dx + (size_t)p * cols;
+            a.y = dy + (size_t)p * rows;
+            a.positions = 1;
+            a.epilogue = epilogue;
+            a.bias = bias;
+            a.residual = residual;
+            a.err = ctx->d_err;
+            a.use_pdl = use_pdl;
+            cudaError_t e = launch_kq_gemv(a, stream);
+            if (e != cudaSuccess) return cuda_fail(e, "launch K-quant MatVec");
+        }
+        return SATORI_OK;
+    }
     const int per_launch = order == SATORI_ORDER_BATCH ? 8 : 1;
     for (int p0 = 0; p0 < positions; p0 += per_launch) {
         const int np = std::min(per_launch, positions - p0);
@@ -176,6 +214,8 @@ int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int 
             a.norm_eps = norm_eps;
             if (xp) a.xp = *xp;
             if (xw) a.xw = *xw;
+            a.next_payload = hint;
+            a.next_bytes = hint_bytes;
             DecodePlan dp = {};
             if (stream_kernel_enabled()) {
                 dp = plan_gemv_stream(a, ctx->sm_count, ctx->smem_optin);

@@ -20,6 +20,10 @@ struct satori_ctx {
     int *d_status = nullptr;           // validation status scratch
     float *attn_scratch = nullptr;     // grow-only partial records for one-shot attention calls
     size_t attn_scratch_floats = 0;
+    // Weights the next MatVec of a captured sequence will stream: the current launch prefetches their
+    // head into L2 during its tail.  Set by the caller just before run_gemv, consumed (cleared) by it.
+    const uint8_t *next_payload = nullptr;
+    size_t next_bytes = 0;
 };
 
 struct satori_matrix {

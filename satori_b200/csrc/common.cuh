@@ -214,6 +214,13 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
+// L2 prefetch of a global range (no shared-memory destination, nothing to wait for).  src and bytes must
+// be multiples of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(src), "r"(bytes) : "memory");
+}
+
 // --------------------------------------------------------------------------- PDL
 // Programmatic dependent launch: wait for the producer grid's memory to be visible / let the
 // next grid start its prologue.  Both are no-ops when the launch did not use PDL.

@@ -33,6 +33,8 @@ struct GemvArgs {
     float norm_eps;
     XPush xp;                // sharded step: push the epilogue's output to the peers (gemv_rows only)
     XWait xw;                // sharded step: wait for the peers' slices of x first (gemv_rows only)
+    const uint8_t *next_payload;  // gemv_stream: weights of the next MatVec, whose head this launch
+    size_t next_bytes;            // prefetches into L2 once its own last stage has landed (0: none)
 };
 
 // Geometry the host chooses for one launch.
@@ -68,6 +70,14 @@ bool gemv_fused_takes(int rows, int cols, int format, int epilogue, int sm_count
 DecodePlan plan_gemv_decode(const GemvArgs &a, int sm_count, size_t smem_limit);
 cudaError_t launch_gemv_decode(const GemvArgs &a, const DecodePlan &plan, cudaStream_t stream);
 cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &plan, cudaStream_t stream);
+// gemv_kquant.cu: GGUF Q4_K / Q6_K (batch order: Q8_K activations and exact integer products; scalar and
+// execute orders in FP32), their row decode and validation.
+bool is_kquant(int format);
+cudaError_t launch_kq_gemv(const GemvArgs &a, cudaStream_t stream);
+cudaError_t launch_kq_decode_row(const uint8_t *payload, int cols, int format, const int *row_dev, int row_host,
+                                 float *out, cudaStream_t stream);
+cudaError_t launch_kq_validate(const uint8_t *payload, int rows, int cols, int format, int *status_dev,
+                               cudaStream_t stream);
 int gemv_block_bytes(int format);
 int gemv_block_elems(int format);
 

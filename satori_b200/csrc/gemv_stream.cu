@@ -70,10 +70,13 @@ struct StreamArgs {
     float norm_eps;
     XPush xp;
     XWait xw;
+    const uint8_t *next;      // head of the next MatVec's weights, prefetched into L2 in the tail
+    uint32_t next_chunk;      // bytes of it per CTA (a multiple of 16)
+    size_t next_bytes;
 };
 
 struct StHeader {
-    uint64_t *full, *empty, *dfull, *dfree;
+    uint64_t *full, *empty, *dfull, *dfree, *xready;
     double *red;
     volatile int *abort_flag;
     __device__ explicit StHeader(uint8_t *smem)
@@ -82,11 +85,12 @@ struct StHeader {
         empty = full + kStMaxStages;
         dfull = empty + kStMaxStages;
         dfree = dfull + kStTables;
-        red = reinterpret_cast<double *>(dfree + kStTables);
+        xready = dfree + kStTables;
+        red = reinterpret_cast<double *>(xready + 1);
         abort_flag = reinterpret_cast<volatile int *>(red + 8);
     }
 };
-static_assert((2 * kStMaxStages + 2 * kStTables + 8) * 8 + 4 <= kStHeader, "stream header");
+static_assert((2 * kStMaxStages + 2 * kStTables + 1 + 8) * 8 + 4 <= kStHeader, "stream header");
 
 __device__ __forceinline__ bool st_wait(uint64_t *bar, uint32_t parity, const StHeader &h, unsigned *err)
 {
@@ -125,6 +129,17 @@ __device__ __forceinline__ void st_compute(const StreamArgs &a, uint8_t *smem, i
                                     rms_apply(xv[q].z, scale, w4.z), rms_apply(xv[q].w, scale, w4.w));
             }
         }
+    }
+    // Release the weight copies only once this warp's activations are in registers: issued behind the
+    // copies, the activation loads would wait for the whole ring fill to reach the SM.  (Adding the 32
+    // values makes every load complete before the arrival.)
+    {
+        float all = 0.0f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) all += (xv[q].x + xv[q].y) + (xv[q].z + xv[q].w);
+        asm volatile("" ::"f"(all));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(h.xready);
     }
     // This lane's word of row 0 (row set `set`) in slot 0, and its term-table column.
     const uint8_t *lrow = ring + set * G::RB + (b * G::BB - PH);
@@ -201,6 +216,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, MINB) gemv_stream_kernel(const 
             mbar_init(&h.dfull[k], CW);
             mbar_init(&h.dfree[k], 1);
         }
+        mbar_init(h.xready, CW);
         fence_mbar_init();
     }
     __syncthreads();
@@ -212,8 +228,12 @@ __global__ void __launch_bounds__((CW + 2) * 32, MINB) gemv_stream_kernel(const 
         bulk_g2s(ring + (size_t)s * G::SLOT, a.payload + ((size_t)row0 + (size_t)i * G::R) * G::RB, bytes,
                  &h.full[s]);
     };
-    if (producer && lane == 0)
-        for (int i = 0; i < min(S, nst); ++i) issue(i, i);
+    // Weights never depend on the previous kernel: the first stage starts moving into L2 before the
+    // programmatic-launch wait (only the first: requested together, the stages of every CTA would share
+    // the bandwidth and each CTA's first stage would land last); the copies into shared memory follow the
+    // activation loads.
+    if (producer && lane == 0 && nst > 0)
+        bulk_prefetch_l2(a.payload + (size_t)row0 * G::RB, (uint32_t)(min(G::R, nrows_cta) * G::RB));
     if (a.use_pdl) {
         pdl_launch_dependents();
         pdl_wait();
@@ -229,6 +249,8 @@ __global__ void __launch_bounds__((CW + 2) * 32, MINB) gemv_stream_kernel(const 
 
     if (producer) {
         if (lane != 0) return;
+        if (!st_wait(h.xready, 0, h, a.err)) return;
+        for (int i = 0; i < min(S, nst); ++i) issue(i, i);
         int i = S, s = 0;
         uint32_t par = 0;
         for (; i < nst; ++i) {
@@ -243,6 +265,17 @@ __global__ void __launch_bounds__((CW + 2) * 32, MINB) gemv_stream_kernel(const 
             // Copies already issued land before the CTA's shared memory goes away.
             const int last = min(i, nst) - 1;
             for (int k = max(0, last - S + 1); k <= last; ++k) mbar_wait_bounded(&h.full[k % S], (uint32_t)((k / S) & 1));
+            return;
+        }
+        // Once this CTA's last stage has landed, DRAM has room: start the next MatVec's weights (this CTA's
+        // share of their head) on their way into L2.
+        if (a.next && nst > 0 && mbar_wait_bounded(&h.full[(nst - 1) % S], (uint32_t)(((nst - 1) / S) & 1))) {
+            const size_t begin = (size_t)blockIdx.x * a.next_chunk;
+            if (begin < a.next_bytes) {
+                const size_t end = min(a.next_bytes, begin + a.next_chunk);
+                for (size_t o = begin; o < end; o += 65536)
+                    bulk_prefetch_l2(a.next + o, (uint32_t)min((size_t)65536, end - o));
+            }
         }
         return;
     }
@@ -414,6 +447,16 @@ cudaError_t launch_gemv_stream(const GemvArgs &a, const DecodePlan &plan, cudaSt
     g.norm_eps = a.norm_eps;
     g.xp = a.xp;
     g.xw = a.xw;
+    g.next = nullptr;
+    g.next_chunk = 0;
+    g.next_bytes = 0;
+    if (a.next_payload && a.next_bytes >= 16) {
+        // At most 32 MB of the next weights (a fraction of L2), split evenly over the CTAs.
+        g.next = a.next_payload;
+        g.next_bytes = std::min(a.next_bytes, (size_t)32 << 20) & ~(size_t)15;
+        const size_t chunk = (g.next_bytes + plan.grid - 1) / plan.grid;
+        g.next_chunk = (uint32_t)((chunk + 15) & ~(size_t)15);
+    }
     const cudaError_t e = opt_in_smem(reinterpret_cast<const void *>(v->kernel), plan.smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};

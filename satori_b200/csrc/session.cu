@@ -190,6 +190,12 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
         pending = false;
         return launch_xwait(s, st);
     };
+    // The head of the next projection's weights goes into L2 while the current one finishes.
+    auto hint = [&](const DevMatrix &m) {
+        s->ctx->next_payload = s->prefetch_next ? m.payload : nullptr;
+        s->ctx->next_bytes = m.payload ? payload_bytes(m.rows, m.cols, m.format) : 0;
+    };
+    auto first_projection = [&](const Layer &L) -> const DevMatrix & { return L.qkv.payload ? L.qkv : L.q; };
     auto carries = [&](int rows, int cols, int fmt, int epi) {
         return xf && gemv_fused_takes(rows, cols, fmt, epi, s->ctx->sm_count, s->ctx->smem_optin);
     };
@@ -203,6 +209,7 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
             TRYCUDA(launch_rmsnorm(s->d_hidden, L.attn_norm, H, s->eps, s->d_normed, st, pdl), "rmsnorm");
         }
         if (L.qkv.payload) {
+            hint(L.o);
             TRY(run_gemv(s->ctx, L.qkv.payload, L.qkv.rows, H, L.qkv.format, SATORI_ORDER_BATCH,
                          L.qkv_norm ? s->d_hidden : s->d_normed, s->d_qkv, 1, L.qkv_bias ? kEpiBias : kEpiNone,
                          L.qkv_bias, nullptr, st, pdl, L.qkv_norm ? L.attn_norm : nullptr, s->eps, nullptr,
@@ -266,11 +273,13 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
         }
         if (carries(s->h1 - s->h0, qw, L.o.format, kEpiResidual)) {
             const XPush xp = session_xpush(s, s->d_hidden + s->h0);
+            hint(L.gu.payload ? L.gu : L.gate);
             TRY(run_gemv(s->ctx, L.o.payload, s->h1 - s->h0, qw, L.o.format, SATORI_ORDER_BATCH, s->d_ctx,
                          s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl, nullptr, 0.0f,
                          &xp));
             pending = true;
         } else {
+            hint(L.gu.payload ? L.gu : L.gate);
             TRY(run_gemv(s->ctx, L.o.payload, s->h1 - s->h0, qw, L.o.format, SATORI_ORDER_BATCH, s->d_ctx,
                          s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl));
             TRY(session_exchange(s, s->d_hidden, (size_t)s->h0, (size_t)(s->h1 - s->h0), st));
@@ -279,6 +288,7 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
         if (L.gu.payload) {
             // ffn_norm runs inside the launch: every CTA forms the same norm of the residual.
             const XPush xp = xf ? session_xpush(s, s->d_act + s->f0) : XPush{};
+            hint(L.down);
             TRY(run_gemv(s->ctx, L.gu.payload, 2 * nf, H, L.gu.format, SATORI_ORDER_BATCH, s->d_hidden,
                          s->d_act + s->f0, 1, kEpiSwiGlu, nullptr, nullptr, st, pdl, L.ffn_norm, s->eps,
                          xf ? &xp : nullptr, take_wait()));
@@ -296,14 +306,17 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
             TRYCUDA(launch_swiglu(s->d_gate, s->d_up, nf, s->d_act + s->f0, st, pdl), "swiglu");
             TRY(session_exchange(s, s->d_act, (size_t)s->f0, (size_t)nf, st));
         }
+        const DevMatrix &after_down = l + 1 < s->layers ? first_projection(s->layer[l + 1]) : s->output;
         if (carries(s->h1 - s->h0, s->ffn, L.down.format, kEpiResidual)) {
             const XPush xp = session_xpush(s, s->d_hidden + s->h0);
+            hint(after_down);
             TRY(run_gemv(s->ctx, L.down.payload, s->h1 - s->h0, s->ffn, L.down.format, SATORI_ORDER_BATCH,
                          s->d_act, s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl,
                          nullptr, 0.0f, &xp, take_wait()));
             pending = true;
         } else {
             TRY(flush_wait());
+            hint(after_down);
             TRY(run_gemv(s->ctx, L.down.payload, s->h1 - s->h0, s->ffn, L.down.format, SATORI_ORDER_BATCH,
                          s->d_act, s->d_proj + s->h0, 1, kEpiResidual, nullptr, s->d_hidden + s->h0, st, pdl));
             TRY(session_exchange(s, s->d_hidden, (size_t)s->h0, (size_t)(s->h1 - s->h0), st));
@@ -313,10 +326,12 @@ static int enqueue_step(satori_session *s, cudaStream_t st)
     TRYCUDA(launch_rmsnorm(s->d_hidden, s->output_norm, H, s->eps, s->d_final, st, pdl), "final norm");
     if (carries(s->v1 - s->v0, H, s->output.format, kEpiNone)) {
         const XPush xp = session_xpush(s, s->d_logits + s->v0);
+        hint(first_projection(s->layer[0]));
         TRY(run_gemv(s->ctx, s->output.payload, s->v1 - s->v0, H, s->output.format, SATORI_ORDER_BATCH, s->d_final,
                      s->d_logits + s->v0, 1, kEpiNone, nullptr, nullptr, st, pdl, nullptr, 0.0f, &xp));
         pending = true;
     } else {
+        hint(first_projection(s->layer[0]));
         TRY(run_gemv(s->ctx, s->output.payload, s->v1 - s->v0, H, s->output.format, SATORI_ORDER_BATCH, s->d_final,
                      s->d_logits + s->v0, 1, kEpiNone, nullptr, nullptr, st, pdl));
         TRY(session_exchange(s, s->d_logits, (size_t)s->v0, (size_t)(s->v1 - s->v0), st));
@@ -487,6 +502,8 @@ satori_session *session_new(satori_ctx *ctx, const satori_model_desc *d, int con
     s->use_pdl = 1;
     const char *fuse = getenv("SATORI_FUSE");
     s->fuse = !(fuse && strcmp(fuse, "0") == 0);
+    const char *pf = getenv("SATORI_PREFETCH_NEXT");
+    s->prefetch_next = !(pf && strcmp(pf, "0") == 0);
     return s;
 }
 

@@ -48,6 +48,8 @@ struct satori_session {
     int position = 0;
     int use_pdl = 1;
     int fuse = 1;                    // stack q/k/v and interleave gate/up (SATORI_FUSE=0 keeps them apart)
+    int prefetch_next = 1;           // each projection prefetches the next one's weights into L2
+                                     // (SATORI_PREFETCH_NEXT=0 turns it off)
     size_t weight_bytes = 0;
 
     std::vector<Layer> layer;

@@ -61,6 +61,11 @@ def main(ref: str) -> None:
         }
 
     ops = os.path.join(ref, "fixtures", "operators")
+    # K-quant fixtures, whole: Q4_K / Q6_K decode and dot (independent FP64), the Q8_K quantizer's exact
+    # bytes with the Q4_K x Q8_K product, the Q6_K x Q8_K product, and blocks of two real tensors.
+    kquants = {}
+    for name in ("q4k-v1", "q6k-v1", "q8k-v1", "q6k-q8k-v1", "k-real-v1"):
+        kquants[name.replace("-", "_")] = json.load(open(os.path.join(ops, name + ".json")))
     v1 = json.load(open(os.path.join(ops, "transformer-v1.json")))
     v2 = json.load(open(os.path.join(ops, "transformer-v2.json")))
     ab = json.load(open(os.path.join(ops, "attention-boundaries-v1.json")))
@@ -75,6 +80,7 @@ def main(ref: str) -> None:
         "tolerance_operator": {"abs": 2e-6, "rel": 2e-6, "stated_in": "QwenOperatorTests.cs:24; TransformerOpsTests.cs:16"},
         "gguf_v1": gguf,
         "gguf_v1_files": {"source": "fixtures/gguf/v1/*.gguf and manifest.json", "files": gguf_files},
+        "kquants": {"source": "fixtures/operators/{q4k,q6k,q8k,q6k-q8k,k-real}-v1.json", **kquants},
         "transformer_v1": v1,
         "transformer_v2": v2,
         "attention_boundaries_v1": {"source": "fixtures/operators/attention-boundaries-v1.json",

@@ -276,3 +276,128 @@ def test_greedy_selector(oracle_lib):
     assert oracle_lib.greedy_select([1.0, 3.0, 3.0, -1.0]) == 1
     with pytest.raises(oracle_lib.OracleError):
         oracle_lib.greedy_select([1.0, np.nan])
+
+
+# ---------------------------------------------------------------- K-quants (Q4_K, Q6_K, Q8_K)
+def _kq():
+    return golden()["kquants"]
+
+
+def _close(actual, reference, abs_tol, rel_tol):
+    return abs(float(actual) - reference) <= abs_tol + rel_tol * abs(reference)
+
+
+@pytest.mark.parametrize("name,fmt", [("q4k_v1", 12), ("q6k_v1", 14)])
+def test_k_decode_and_dot_match_reference(oracle_lib, name, fmt):
+    """Q4KCodecTests / Q6KCodecTests (DecodedWeightsMatchReference, DotMatchesReference): the independent
+    FP64 decode within 1e-3 + 1e-4 |w| and the scalar dot within 1e-2 + 1e-4 |dot|."""
+    for case in _kq()[name]["cases"]:
+        block = bytes.fromhex(case["block_hex"])
+        w = oracle_lib.k_decode_row(block, 256, fmt)
+        for a, r in zip(w, case["weights"]):
+            assert _close(a, r, 1e-3, 1e-4), (case["name"], a, r)
+        x = np.array(case["input"], np.float32)
+        y = oracle_lib.k_matvec(block, 1, 256, fmt, x, order="scalar")
+        assert _close(y[0], case["dot"], 1e-2, 1e-4), (case["name"], y[0], case["dot"])
+        y2 = oracle_lib.k_matvec(block, 1, 256, fmt, x, order="avx2")
+        assert _close(y2[0], case["dot"], 1e-2, 1e-4), (case["name"], "avx2")
+
+
+def test_zero_q4k_block_decodes_to_zeros(oracle_lib):
+    zero = next(c for c in _kq()["q4k_v1"]["cases"] if c["name"] == "zero")
+    assert np.all(oracle_lib.k_decode_row(bytes.fromhex(zero["block_hex"]), 256, 12) == 0)
+
+
+def test_q8k_quantizer_bytes_and_q4k_integer_product(oracle_lib):
+    """Q8KCodecTests (QuantizerMatchesTheReferenceBytes, ScaleAndGroupSums, IntegerProductMatchesTheReferenceDot):
+    the quantized block equals ggml's bytes exactly; the Q4_K x Q8_K product within 1e-3 + 1e-4 |dot|."""
+    import struct
+    for case in _kq()["q8k_v1"]["cases"]:
+        x = np.array(case["input"], np.float32)
+        q = oracle_lib.q8k_quantize_row(x)
+        assert q.tobytes() == bytes.fromhex(case["block_hex"]), case["name"]
+        assert list(q[4:260].view(np.int8)) == case["codes"]
+        assert list(q[260:292].view(np.int16)) == case["bsums"]
+        scale = struct.unpack("<f", q[:4].tobytes())[0]
+        assert abs(scale - case["scale"]) <= 1e-6 * max(1.0, abs(case["scale"]))
+        w = bytes.fromhex(case["weights_hex"])
+        dot, mins = oracle_lib.k_int_dot(w, 12, q)
+        d = oracle_lib.half_to_float(w[0] | (w[1] << 8))
+        dmin = oracle_lib.half_to_float(w[2] | (w[3] << 8))
+        value = np.float32(np.float32(d) * np.float32(scale)) * np.float32(dot) - \
+            np.float32(np.float32(dmin) * np.float32(scale)) * np.float32(mins)
+        assert _close(value, case["dot"], 1e-3, 1e-4), case["name"]
+
+
+def test_q6k_integer_product(oracle_lib):
+    """Q6KQuantizedProductTests.IntegerProductMatchesTheIndependentReference and the decoder composition."""
+    import struct
+    cases = _kq()["q6k_q8k_v1"]["cases"]
+    assert len(cases) == 5
+    for case in cases:
+        w = bytes.fromhex(case["weights_hex"])
+        a = bytes.fromhex(case["activation_hex"])
+        scale = struct.unpack("<f", a[:4])[0]
+        dot, _ = oracle_lib.k_int_dot(w, 14, a)
+        d = oracle_lib.half_to_float(w[208] | (w[209] << 8))
+        value = np.float32(np.float32(scale) * np.float32(d)) * np.float32(dot)
+        assert _close(value, case["dot"], 1e-3, 1e-4), case["name"]
+        decoded = oracle_lib.k_decode_row(w, 256, 14).astype(np.float64)
+        codes = np.frombuffer(a[4:260], np.int8).astype(np.float64)
+        assert _close(value, float(decoded @ codes) * scale, 1e-3, 1e-4)
+
+
+def test_real_tensor_blocks(oracle_lib):
+    """KParityTests.RealTensorBlocksDecodeToTheIndependentReference: blocks of a real Q4_K_M model."""
+    for case in _kq()["k_real_v1"]["cases"]:
+        fmt = 12 if case["name"].startswith("q4k:") else 14
+        raw = bytes.fromhex(case["block_hex"])
+        w = oracle_lib.k_decode_row(raw, 256 * case["blocks"], fmt)
+        for a, r in zip(w, case["weights"]):
+            assert _close(a, r, 1e-3, 1e-4), case["name"]
+        x = np.array(case["input"], np.float32)
+        bb = 144 if fmt == 12 else 210
+        for b in range(case["blocks"]):
+            y = oracle_lib.k_matvec(raw[b * bb:(b + 1) * bb], 1, 256, fmt, x, order="scalar")
+            assert _close(y[0], case["dots"][b], 1e-2, 1e-4), (case["name"], b)
+
+
+@pytest.mark.parametrize("cols,threads", [(3584, 1), (18944, 8)])
+def test_q4k_batch_matches_block_products(oracle_lib, cols, threads):
+    """KParityTests.Q4DecodeMatchesThePublicQuantizedCodecs: the batched integer path equals the per-block
+    quantized products (17 rows cycling the fixture blocks, sin input)."""
+    blocks_hex = [bytes.fromhex(c["block_hex"]) for c in _kq()["q4k_v1"]["cases"]]
+    rows, nb = 17, cols // 256
+    payload = b"".join(blocks_hex[(r + b) % len(blocks_hex)] for r in range(rows) for b in range(nb))
+    x = np.sin(np.arange(cols) * 0.017).astype(np.float32)
+    got = oracle_lib.k_matvec(payload, rows, cols, 12, x, order="batch", threads=threads)
+    act = oracle_lib.q8k_quantize_row(x)
+    import struct
+    for r in range(rows):
+        expected = 0.0
+        for b in range(nb):
+            a = act[b * 292:(b + 1) * 292]
+            s = struct.unpack("<f", a[:4].tobytes())[0]
+            blk = payload[(r * nb + b) * 144:(r * nb + b + 1) * 144]
+            dot, mins = oracle_lib.k_int_dot(blk, 12, a)
+            d = oracle_lib.half_to_float(blk[0] | (blk[1] << 8))
+            dm = oracle_lib.half_to_float(blk[2] | (blk[3] << 8))
+            expected += float(np.float32(np.float32(d) * np.float32(s)) * np.float32(dot)
+                              - np.float32(np.float32(dm) * np.float32(s)) * np.float32(mins))
+        assert _close(got[r], expected, 1e-3, 1e-5), r
+
+
+def test_k_validation(oracle_lib):
+    """Q4KCodecTests / Q6KCodecTests.NonFiniteSuperBlockScaleIsRejected and the shape rule."""
+    p = np.zeros(144, np.uint8)
+    p[1] = 0x7C
+    assert oracle_lib.k_validate(p, 1, 256, 12) == oracle_lib.ERR_INVALID_DATA
+    p = np.zeros(144, np.uint8)
+    p[3] = 0x7C
+    assert oracle_lib.k_validate(p, 1, 256, 12) == oracle_lib.ERR_INVALID_DATA
+    p = np.zeros(210, np.uint8)
+    p[209] = 0x7C
+    assert oracle_lib.k_validate(p, 1, 256, 14) == oracle_lib.ERR_INVALID_DATA
+    assert oracle_lib.k_validate(np.zeros(210, np.uint8), 1, 256, 14) == oracle_lib.OK
+    with pytest.raises(oracle_lib.OracleError):
+        oracle_lib.k_geometry(1, 128, 14)
