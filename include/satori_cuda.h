@@ -46,7 +46,12 @@ typedef enum satori_format {
     SATORI_Q6_K = 14,   /* GGUF Q6_K: 256-weight super-blocks of 210 bytes (Q6KCodec.cs) */
     SATORI_T2_64 = 64,
     SATORI_T2_128 = 128,
-    SATORI_T2_256 = 256
+    SATORI_T2_256 = 256,
+    /* Ternary bitplane (docs/ternary-bitplane-v1.md, src/Satori.Core/TernaryBitplaneMatrix.cs): the same blocks
+     * as Ternary2 with a positive and a negative bit plane instead of 2-bit codes. */
+    SATORI_TB_64 = 1064,
+    SATORI_TB_128 = 1128,
+    SATORI_TB_256 = 1256
 } satori_format;
 
 /* Which reference routine's FP32 operation order a MatVec reproduces (bit for bit). */

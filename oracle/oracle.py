@@ -249,6 +249,36 @@ def k_int_dot(block, fmt: int, activation):
     return dot.value, mins.value
 
 
+# ---------------------------------------------------------------- ternary bitplane (STB1)
+def tb_from_t2(t2, rows: int, cols: int, bs: int) -> np.ndarray:
+    _, _, ln = t2_geometry(rows, cols, bs)
+    d = _c_u8(t2)
+    out = np.zeros(ln, dtype=np.uint8)
+    _check(lib().so_tb_from_t2(_u8(d), rows, cols, bs, _u8(out)), "tb_from_t2")
+    return out
+
+
+def tb_to_t2(tb, rows: int, cols: int, bs: int) -> np.ndarray:
+    _, _, ln = t2_geometry(rows, cols, bs)
+    d = _c_u8(tb)
+    out = np.zeros(ln, dtype=np.uint8)
+    _check(lib().so_tb_to_t2(_u8(d), rows, cols, bs, _u8(out)), "tb_to_t2")
+    return out
+
+
+def tb_validate(data, rows: int, cols: int, bs: int) -> int:
+    d = _c_u8(data)
+    return lib().so_tb_validate(_u8(d), C.c_int64(d.size), rows, cols, bs)
+
+
+def tb_matvec(data, rows: int, cols: int, bs: int, x, order: str = "avx2") -> np.ndarray:
+    d, xv = _c_u8(data), _c_f32(x)
+    y = np.zeros(rows, dtype=np.float32)
+    fn = lib().so_tb_matvec_avx2 if order == "avx2" else lib().so_tb_matvec_scalar
+    _check(fn(_u8(d), rows, cols, bs, _f32(xv), _f32(y)), "tb_matvec")
+    return y
+
+
 # ---------------------------------------------------------------- operators
 def rmsnorm(x, w, eps: float) -> np.ndarray:
     xv, wv = _c_f32(x), _c_f32(w)

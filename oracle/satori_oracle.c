@@ -1193,3 +1193,135 @@ int so_k_matvec_batch(const uint8_t *data, int rows, int cols, int fmt, const fl
     free(act);
     return SO_OK;
 }
+
+/* ------------------------------------------------------------------------- */
+/* Ternary bitplane (STB1): docs/ternary-bitplane-v1.md                      */
+/* ------------------------------------------------------------------------- */
+
+/* TernaryBitplaneMatrix.FromTernary2 (TernaryBitplaneMatrix.cs:18-36): scale copied, code 1 -> P bit,
+ * code 2 -> N bit, same blocks and padding. */
+int so_tb_from_t2(const uint8_t *t2, int rows, int cols, int bs, uint8_t *out)
+{
+    int bpr, bb; int64_t len;
+    int rc = so_t2_geometry(rows, cols, bs, &bpr, &bb, &len);
+    if (rc) return rc;
+    int plane = bs / 8;
+    memset(out, 0, (size_t)len);
+    for (int64_t off = 0; off < len; off += bb) {
+        memcpy(out + off, t2 + off, 4);
+        for (int i = 0; i < bs; i++) {
+            int code = (t2[off + 4 + i / 4] >> (2 * (i % 4))) & 3;
+            if (code != 0) out[off + 4 + (code == 2 ? plane : 0) + i / 8] |= (uint8_t)(1 << (i % 8));
+        }
+    }
+    return SO_OK;
+}
+
+/* TernaryBitplaneMatrix.ToTernary2 (:38-55): P -> 01, N -> 10. */
+int so_tb_to_t2(const uint8_t *tb, int rows, int cols, int bs, uint8_t *out)
+{
+    int bpr, bb; int64_t len;
+    int rc = so_t2_geometry(rows, cols, bs, &bpr, &bb, &len);
+    if (rc) return rc;
+    int plane = bs / 8;
+    memset(out, 0, (size_t)len);
+    for (int64_t off = 0; off < len; off += bb) {
+        memcpy(out + off, tb + off, 4);
+        for (int i = 0; i < bs; i++) {
+            int p = (tb[off + 4 + i / 8] >> (i % 8)) & 1;
+            int n = (tb[off + 4 + plane + i / 8] >> (i % 8)) & 1;
+            out[off + 4 + i / 4] |= (uint8_t)((p | n << 1) << (2 * (i % 4)));
+        }
+    }
+    return SO_OK;
+}
+
+/* TernaryBitplaneMatrix.Validate (:66-87) */
+int so_tb_validate(const uint8_t *data, int64_t len, int rows, int cols, int bs)
+{
+    int bpr, bb; int64_t want;
+    int rc = so_t2_geometry(rows, cols, bs, &bpr, &bb, &want);
+    if (rc) return rc;
+    if (len != want) return SO_ERR_ARGUMENT;
+    int plane = bs / 8;
+    for (int row = 0; row < rows; row++)
+        for (int b = 0; b < bpr; b++) {
+            const uint8_t *blk = data + ((int64_t)row * bpr + b) * bb;
+            float scale = rdf32(blk);
+            if (!isfinite_f(scale) || scale < 0 || f2u(scale) == 0x80000000u) return SO_ERR_ARGUMENT;
+            int count = bs < cols - b * bs ? bs : cols - b * bs;
+            for (int i = 0; i < plane; i++) {
+                uint8_t p = blk[4 + i], n = blk[4 + plane + i];
+                int valid = count - i * 8;
+                valid = valid < 0 ? 0 : valid > 8 ? 8 : valid;
+                int padding = ~((1 << valid) - 1);
+                if ((p & n) != 0 || ((p | n) & padding) != 0 || (scale == 0 && (p | n) != 0)) return SO_ERR_ARGUMENT;
+            }
+        }
+    return SO_OK;
+}
+
+/* TernaryBitplaneMatVec.ExecuteScalar (TernaryBitplaneMatVec.cs:24-47): sequential +x / -x per block,
+ * total += scale * sum. */
+int so_tb_matvec_scalar(const uint8_t *data, int rows, int cols, int bs, const float *x, float *y)
+{
+    int bpr, bb; int64_t len;
+    int rc = so_t2_geometry(rows, cols, bs, &bpr, &bb, &len);
+    if (rc) return rc;
+    int plane = bs / 8;
+    for (int row = 0; row < rows; row++) {
+        float total = 0;
+        for (int b = 0; b < bpr; b++) {
+            const uint8_t *blk = data + ((int64_t)row * bpr + b) * bb;
+            int column = b * bs, count = bs < cols - column ? bs : cols - column;
+            float sum = 0;
+            for (int i = 0; i < count; i++) {
+                int mask = 1 << (i % 8);
+                if (blk[4 + i / 8] & mask) sum += x[column + i];
+                else if (blk[4 + plane + i / 8] & mask) sum -= x[column + i];
+            }
+            total += rdf32(blk) * sum;
+        }
+        y[row] = total;
+    }
+    return SO_OK;
+}
+
+/* TernaryBitplaneAvx2Kernel.Execute (TernaryBitplaneAvx2Kernel.cs:18-52): eight lanes of
+ * AndNot(zero, x ^ sign), the fixed horizontal sum, a scalar tail, total += scale * partial. */
+int so_tb_matvec_avx2(const uint8_t *data, int rows, int cols, int bs, const float *x, float *y)
+{
+    int bpr, bb; int64_t len;
+    int rc = so_t2_geometry(rows, cols, bs, &bpr, &bb, &len);
+    if (rc) return rc;
+    int plane = bs / 8;
+    const __m256i shifts = _mm256_setr_epi32(0, 1, 2, 3, 4, 5, 6, 7);
+    const __m256i active = _mm256_set1_epi32(0x101), negative = _mm256_set1_epi32(0x100);
+    for (int row = 0; row < rows; row++) {
+        float total = 0;
+        for (int b = 0; b < bpr; b++) {
+            const uint8_t *blk = data + ((int64_t)row * bpr + b) * bb;
+            int column = b * bs, count = bs < cols - column ? bs : cols - column;
+            __m256 acc = _mm256_setzero_ps();
+            int i = 0;
+            for (; i <= count - 8; i += 8) {
+                uint32_t packed = (uint32_t)(blk[4 + i / 8] | blk[4 + plane + i / 8] << 8);
+                __m256i lanes = _mm256_srlv_epi32(_mm256_set1_epi32((int)packed), shifts);
+                __m256i zero = _mm256_cmpeq_epi32(_mm256_and_si256(lanes, active), _mm256_setzero_si256());
+                __m256i sign = _mm256_slli_epi32(_mm256_and_si256(lanes, negative), 23);
+                __m256 values = _mm256_loadu_ps(x + column + i);
+                acc = _mm256_add_ps(acc, _mm256_andnot_ps(_mm256_castsi256_ps(zero),
+                                                          _mm256_xor_ps(values, _mm256_castsi256_ps(sign))));
+            }
+            float partial = hsum256(acc);
+            for (; i < count; i++) {
+                int mask = 1 << (i % 8);
+                if (blk[4 + i / 8] & mask) partial += x[column + i];
+                else if (blk[4 + plane + i / 8] & mask) partial -= x[column + i];
+            }
+            total += rdf32(blk) * partial;
+        }
+        y[row] = total;
+    }
+    return SO_OK;
+}

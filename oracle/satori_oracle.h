@@ -79,6 +79,12 @@ int so_q8k_quantize_row(const float *x, int cols, uint8_t *out);
 int so_k_int_dot(const uint8_t *block, int fmt, const uint8_t *activation, int32_t *dot, int32_t *min_total);
 int so_k_matvec_batch(const uint8_t *data, int rows, int cols, int fmt, const float *x, int positions, float *y,
                       int threads);
+/* Ternary bitplane STB1 (TernaryBitplaneMatrix.cs, TernaryBitplaneMatVec.cs, TernaryBitplaneAvx2Kernel.cs) */
+int so_tb_from_t2(const uint8_t *t2, int rows, int cols, int bs, uint8_t *out);
+int so_tb_to_t2(const uint8_t *tb, int rows, int cols, int bs, uint8_t *out);
+int so_tb_validate(const uint8_t *data, int64_t len, int rows, int cols, int bs);
+int so_tb_matvec_scalar(const uint8_t *data, int rows, int cols, int bs, const float *x, float *y);
+int so_tb_matvec_avx2(const uint8_t *data, int rows, int cols, int bs, const float *x, float *y);
 int so_q_quantize(const float *w, int rows, int cols, int fmt, uint8_t *out);
 
 /* ---------------- operators (src/Satori.Core/TransformerOps.cs) ---------------- */

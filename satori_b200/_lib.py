@@ -24,6 +24,7 @@ ERR_OUT_OF_MEMORY = 8
 
 Q8_0, Q4_0, T2_64, T2_128, T2_256 = 0, 1, 64, 128, 256
 Q4_K, Q6_K = 12, 14
+TB_64, TB_128, TB_256 = 1064, 1128, 1256
 ORDER_EXECUTE, ORDER_SCALAR, ORDER_BATCH = 0, 1, 2
 
 

@@ -327,6 +327,103 @@ class Ternary2Matrix:
             fh.write(self._data.tobytes())
 
 
+# --------------------------------------------------------------------------- ternary bitplane (STB1)
+_TB_FORMAT = {64: _lib.TB_64, 128: _lib.TB_128, 256: _lib.TB_256}
+
+
+class TernaryBitplaneMatrix:
+    """Ternary weights in the bitplane layout (TernaryBitplaneMatrix.cs, docs/ternary-bitplane-v1.md): the
+    same blocks and scales as Ternary2 with a positive and a negative bit plane per block."""
+
+    def __init__(self, rows: int, columns: int, block_size: int, data: np.ndarray, device: CudaQuantizedMatrix):
+        self.rows, self.columns, self.block_size = rows, columns, block_size
+        self._data = data
+        self.device = device
+
+    @property
+    def byte_length(self) -> int:
+        return self._data.size
+
+    @property
+    def data(self) -> np.ndarray:
+        return self._data
+
+    def copy_data_to(self, destination: np.ndarray) -> None:
+        destination.reshape(-1)[: self._data.size] = self._data
+
+    @staticmethod
+    def from_packed(rows: int, columns: int, block_size: int, payload, ctx: Context | None = None):
+        """TernaryBitplaneMatrix.FromPacked (:57-64): length, scales, planes and padding validated on the
+        device (ArgumentError, like the reference's ArgumentException)."""
+        ctx = ctx or default_context()
+        owned = _u8(payload).copy()
+        if owned.size != ternary2_byte_length(rows, columns, block_size):
+            raise ArgumentError(_lib.ERR_ARGUMENT, "Incorrect bitplane payload length.")
+        dev = CudaQuantizedMatrix(ctx, owned, rows, columns, _TB_FORMAT[block_size])
+        return TernaryBitplaneMatrix(rows, columns, block_size, owned, dev)
+
+    @staticmethod
+    def from_ternary2(matrix: "Ternary2Matrix") -> "TernaryBitplaneMatrix":
+        """TernaryBitplaneMatrix.FromTernary2 (:18-36): scale bytes copied, code 1 -> P bit, code 2 -> N bit."""
+        bs, bb = matrix.block_size, 4 + matrix.block_size // 4
+        src = matrix.data.reshape(-1, bb)
+        codes = np.stack([(src[:, 4:] >> (2 * k)) & 3 for k in range(4)], axis=2).reshape(src.shape[0], bs)
+        out = np.zeros_like(src)
+        out[:, :4] = src[:, :4]
+        out[:, 4:4 + bs // 8] = np.packbits(codes == 1, axis=1, bitorder="little")
+        out[:, 4 + bs // 8:] = np.packbits(codes == 2, axis=1, bitorder="little")
+        return TernaryBitplaneMatrix.from_packed(matrix.rows, matrix.columns, bs, out.reshape(-1), matrix._ctx)
+
+    def to_ternary2(self) -> "Ternary2Matrix":
+        """TernaryBitplaneMatrix.ToTernary2 (:38-55): P -> 01, N -> 10, byte-identical to the original."""
+        bs, bb = self.block_size, 4 + self.block_size // 4
+        src = self._data.reshape(-1, bb)
+        p = np.unpackbits(src[:, 4:4 + bs // 8], axis=1, bitorder="little").astype(np.uint8)
+        n = np.unpackbits(src[:, 4 + bs // 8:], axis=1, bitorder="little").astype(np.uint8)
+        codes = (p | (n << 1)).reshape(src.shape[0], bs // 4, 4)
+        out = np.zeros_like(src)
+        out[:, :4] = src[:, :4]
+        out[:, 4:] = codes[:, :, 0] | (codes[:, :, 1] << 2) | (codes[:, :, 2] << 4) | (codes[:, :, 3] << 6)
+        return Ternary2Matrix.from_packed(self.rows, self.columns, bs, out.reshape(-1), self.device.ctx)
+
+    def save(self, path: str) -> None:
+        """TernaryBitplaneMatrix.Save (:89-97): the STB1 header then the payload; refuses to overwrite."""
+        with open(path, "xb") as fh:
+            fh.write(b"STB1" + stq2_header(self.rows, self.columns, self.block_size)[4:])
+            fh.write(self._data.tobytes())
+
+    @staticmethod
+    def load(path: str, ctx: Context | None = None) -> "TernaryBitplaneMatrix":
+        """TernaryBitplaneMatrix.Load (:99-117) with TernaryBitplaneFileFormat.ReadHeader: any defect of the
+        header, length or payload is an InvalidDataError."""
+        raw = open(path, "rb").read()
+        if len(raw) < _STQ2_HEADER or raw[:4] != b"STB1":
+            raise InvalidDataError(_lib.ERR_INVALID_DATA, "Invalid bitplane file.")
+        rows, cols, bs = stq2_read_header(b"STQ2" + raw[4:32])
+        if len(raw) != _STQ2_HEADER + ternary2_byte_length(rows, cols, bs):
+            raise InvalidDataError(_lib.ERR_INVALID_DATA, "Incorrect bitplane file length.")
+        try:
+            return TernaryBitplaneMatrix.from_packed(rows, cols, bs, np.frombuffer(raw[32:], np.uint8), ctx)
+        except ArgumentError as e:
+            raise InvalidDataError(_lib.ERR_INVALID_DATA, "Invalid bitplane file.") from e
+
+
+class TernaryBitplaneMatVec:
+    """TernaryBitplaneMatVec (TernaryBitplaneMatVec.cs): Execute runs the AVX2-order arithmetic."""
+
+    @staticmethod
+    def execute(matrix: TernaryBitplaneMatrix, input, output: np.ndarray | None = None) -> np.ndarray:
+        _check_t2_vectors(matrix.rows, matrix.columns, input, output)
+        return matrix.device.execute(input, output)
+
+    execute_avx2 = execute
+
+    @staticmethod
+    def execute_scalar(matrix: TernaryBitplaneMatrix, input, output: np.ndarray | None = None) -> np.ndarray:
+        _check_t2_vectors(matrix.rows, matrix.columns, input, output)
+        return matrix.device.execute_scalar(input, output)
+
+
 def stq2_header(rows: int, columns: int, block_size: int) -> bytes:
     """Ternary2FileFormat.WriteHeader (Ternary2FileFormat.cs:9-19)."""
     n = ternary2_byte_length(rows, columns, block_size)

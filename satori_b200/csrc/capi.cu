@@ -77,7 +77,7 @@ int check_dev_error(satori_ctx *ctx)
 bool is_valid_format(int f)
 {
     return f == SATORI_Q8_0 || f == SATORI_Q4_0 || f == SATORI_Q4_K || f == SATORI_Q6_K || f == 64 || f == 128 ||
-           f == 256;
+           f == 256 || is_bitplane(f);
 }
 
 size_t payload_bytes(int rows, int cols, int format)
@@ -132,8 +132,9 @@ int upload_payload(satori_ctx *ctx, const uint8_t *src, bool src_is_device, size
         // Quantized: InvalidDataException (QuantizedMatVec.cs:40).  Ternary2 import from a packed
         // buffer: ArgumentException (Ternary2Matrix.cs:92,98); the mapped STQ2 path rethrows it as
         // InvalidDataException (MappedTernary2Matrix.cs:25-28), which the Python mirror does.
-        return set_error(format <= 1 ? SATORI_ERR_INVALID_DATA : SATORI_ERR_ARGUMENT,
-                         format <= 1 ? "non-finite block scale" : "invalid block scale, weight code or padding");
+        const bool gguf = format <= 1 || is_kquant(format);
+        return set_error(gguf ? SATORI_ERR_INVALID_DATA : SATORI_ERR_ARGUMENT,
+                         gguf ? "non-finite block scale" : "invalid block scale, weight code or padding");
     }
     *out = d;
     return SATORI_OK;
@@ -190,6 +191,34 @@ int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int 
             if (e != cudaSuccess) return cuda_fail(e, "launch K-quant MatVec");
         }
         return SATORI_OK;
+    }
+    if (format >= 64) {
+        // Ternary2 / bitplane: the row-streaming kernel takes the AVX2 order on whole blocks; bitplane
+        // matrices otherwise use the row-per-thread kernel, Ternary2 the general kernel below.
+        if (order == SATORI_ORDER_BATCH)
+            return set_error(SATORI_ERR_NOT_SUPPORTED, "ExecuteBatch is defined for the GGUF formats only");
+        if (epilogue != kEpiNone || norm_w || xp || xw || positions != 1)
+            return set_error(SATORI_ERR_NOT_SUPPORTED, "ternary MatVec takes one position and no epilogue");
+        GemvArgs a = {};
+        a.payload = d_payload;
+        a.rows = rows;
+        a.cols = cols;
+        a.format = format;
+        a.order = order;
+        a.x = dx;
+        a.y = dy;
+        a.positions = 1;
+        a.epilogue = kEpiNone;
+        a.err = ctx->d_err;
+        a.use_pdl = use_pdl;
+        bool taken = false;
+        cudaError_t e = launch_ternary_stream(a, ctx->sm_count, ctx->smem_optin, stream, &taken);
+        if (e != cudaSuccess) return cuda_fail(e, "launch ternary MatVec");
+        if (taken) return SATORI_OK;
+        if (is_bitplane(format)) {
+            e = launch_bitplane_rowwise(a, stream);
+            return e == cudaSuccess ? SATORI_OK : cuda_fail(e, "launch bitplane MatVec");
+        }
     }
     const int per_launch = order == SATORI_ORDER_BATCH ? 8 : 1;
     for (int p0 = 0; p0 < positions; p0 += per_launch) {
@@ -434,7 +463,8 @@ extern "C" int satori_matrix_execute_scalar(satori_matrix *m, const float *x, fl
 
 extern "C" int satori_matrix_execute_batch(satori_matrix *m, const float *x, int positions, float *y)
 {
-    if (m && m->format > 1) return set_error(SATORI_ERR_NOT_SUPPORTED, "ExecuteBatch is defined for Q8_0/Q4_0 only");
+    if (m && m->format >= 64)
+        return set_error(SATORI_ERR_NOT_SUPPORTED, "ExecuteBatch is defined for the GGUF formats only");
     return matrix_execute_host(m, x, y, positions, SATORI_ORDER_BATCH);
 }
 
@@ -445,8 +475,8 @@ extern "C" int satori_matrix_execute_device(satori_matrix *m, const float *dx, f
     if (order < 0 || order > 2) return set_error(SATORI_ERR_ARGUMENT, "bad order %d", order);
     if (order != SATORI_ORDER_BATCH && positions != 1)
         return set_error(SATORI_ERR_ARGUMENT, "only the batch order takes several positions");
-    if (order == SATORI_ORDER_BATCH && m->format > 1)
-        return set_error(SATORI_ERR_NOT_SUPPORTED, "ExecuteBatch is defined for Q8_0/Q4_0 only");
+    if (order == SATORI_ORDER_BATCH && m->format >= 64)
+        return set_error(SATORI_ERR_NOT_SUPPORTED, "ExecuteBatch is defined for the GGUF formats only");
     // Launched with programmatic dependent launch: the kernel streams its weights while the previous
     // kernel on the stream finishes, and waits for it before reading x or writing y.
     return run_gemv(m->ctx, m->d_payload, m->rows, m->cols, m->format, order, dx, dy, positions, kEpiNone, nullptr,

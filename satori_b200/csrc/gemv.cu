@@ -33,11 +33,12 @@ constexpr int kMaxPositions = 8;
 
 __host__ __device__ constexpr int block_bytes_of(int fmt)
 {
-    return fmt == 0 ? 34 : fmt == 1 ? 18 : fmt == SATORI_Q4_K ? 144 : fmt == SATORI_Q6_K ? 210 : 4 + fmt / 4;
+    return fmt == 0 ? 34 : fmt == 1 ? 18 : fmt == SATORI_Q4_K ? 144 : fmt == SATORI_Q6_K ? 210
+         : fmt > 1000 ? 4 + (fmt - 1000) / 4 : 4 + fmt / 4;
 }
 __host__ __device__ constexpr int block_elems_of(int fmt)
 {
-    return fmt <= 1 ? 32 : (fmt == SATORI_Q4_K || fmt == SATORI_Q6_K) ? 256 : fmt;
+    return fmt <= 1 ? 32 : (fmt == SATORI_Q4_K || fmt == SATORI_Q6_K) ? 256 : fmt > 1000 ? fmt - 1000 : fmt;
 }
 
 struct Geo {
@@ -700,6 +701,7 @@ cudaError_t launch_decode_row(const uint8_t *payload, int rows, int cols, int fo
 {
     (void)rows;
     if (is_kquant(format)) return launch_kq_decode_row(payload, cols, format, row_dev, row_host, out, stream);
+    if (is_bitplane(format)) return launch_bitplane_decode_row(payload, cols, format, row_dev, row_host, out, stream);
     const int threads = 256;
     const int blocks = std::min(64, (cols + threads - 1) / threads);
     decode_row_kernel<<<blocks, threads, 0, stream>>>(payload, cols, format, row_dev, row_host, out);
@@ -710,6 +712,7 @@ cudaError_t launch_validate(const uint8_t *payload, int rows, int cols, int form
                             cudaStream_t stream)
 {
     if (is_kquant(format)) return launch_kq_validate(payload, rows, cols, format, status_dev, stream);
+    if (is_bitplane(format)) return launch_bitplane_validate(payload, rows, cols, format, status_dev, stream);
     validate_kernel<<<592, 256, 0, stream>>>(payload, rows, cols, format, status_dev);
     return cudaGetLastError();
 }

@@ -78,6 +78,17 @@ cudaError_t launch_kq_decode_row(const uint8_t *payload, int cols, int format, c
                                  float *out, cudaStream_t stream);
 cudaError_t launch_kq_validate(const uint8_t *payload, int rows, int cols, int format, int *status_dev,
                                cudaStream_t stream);
+// gemv_ternary.cu: the row-streaming ternary MatVec in the AVX2 order for Ternary2 and bitplane matrices
+// (*taken = false when the shape does not qualify; nothing is launched then), and the bitplane fallbacks.
+bool is_bitplane(int format);
+int ternary_block_size(int format);
+cudaError_t launch_ternary_stream(const GemvArgs &a, int sm_count, size_t smem_limit, cudaStream_t stream,
+                                  bool *taken);
+cudaError_t launch_bitplane_rowwise(const GemvArgs &a, cudaStream_t stream);
+cudaError_t launch_bitplane_decode_row(const uint8_t *payload, int cols, int format, const int *row_dev,
+                                       int row_host, float *out, cudaStream_t stream);
+cudaError_t launch_bitplane_validate(const uint8_t *payload, int rows, int cols, int format, int *status_dev,
+                                     cudaStream_t stream);
 int gemv_block_bytes(int format);
 int gemv_block_elems(int format);
 

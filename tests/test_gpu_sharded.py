@@ -78,6 +78,11 @@ CASES = [
     (2, dict(layers=2, hidden=384, ffn=768, q_heads=6, kv_heads=3, head_dim=64, vocab=1000, proj_format=1)),
     (2, dict(layers=3, hidden=192, ffn=384, q_heads=3, kv_heads=1, head_dim=64, vocab=1002, has_bias=False)),
     (4, dict(layers=2, hidden=384, ffn=768, q_heads=6, kv_heads=2, head_dim=64, vocab=1000)),
+    # the 7B shape's head pattern (28 query / 4 KV heads) split over 4 and 8 ranks: 7 or 3.5 query heads per
+    # rank, so at 8 ranks every KV head is cached by the two ranks that share its group
+    (4, dict(layers=2, hidden=896, ffn=1024, q_heads=28, kv_heads=4, head_dim=32, vocab=1000, proj_format=1)),
+    (8, dict(layers=2, hidden=896, ffn=1024, q_heads=28, kv_heads=4, head_dim=32, vocab=1000, proj_format=1)),
+    (8, dict(layers=2, hidden=512, ffn=1024, q_heads=8, kv_heads=8, head_dim=64, vocab=1024)),
 ]
 
 

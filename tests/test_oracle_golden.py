@@ -401,3 +401,49 @@ def test_k_validation(oracle_lib):
     assert oracle_lib.k_validate(np.zeros(210, np.uint8), 1, 256, 14) == oracle_lib.OK
     with pytest.raises(oracle_lib.OracleError):
         oracle_lib.k_geometry(1, 128, 14)
+
+
+# ---------------------------------------------------------------- ternary bitplane (STB1)
+def _tb_kat():
+    p = np.zeros(20, np.uint8)
+    p[0:4] = np.frombuffer(np.float32(0.5).tobytes(), np.uint8)
+    p[4], p[12] = 0x89, 0x14
+    return p
+
+
+def test_bitplane_golden_and_invalid_planes(oracle_lib):
+    """TernaryBitplaneTests.IndependentGoldenAndCodecRejectInvalidPlanes and docs/ternary-bitplane-v1.md's
+    example: scale 0.5, codes [+1,0,-1,+1,-1,0,0,+1] -> P 0x89, N 0x14; ones -> 0.5; Ternary2 bytes 61 42."""
+    p = _tb_kat()
+    assert oracle_lib.tb_validate(p, 1, 8, 64) == oracle_lib.OK
+    ones = np.ones(8, np.float32)
+    assert oracle_lib.tb_matvec(p, 1, 8, 64, ones, "scalar")[0] == 0.5
+    assert oracle_lib.tb_matvec(p, 1, 8, 64, ones, "avx2")[0] == 0.5
+    t2 = oracle_lib.tb_to_t2(p, 1, 8, 64)
+    assert (t2[4], t2[5]) == (0x61, 0x42)
+    assert np.array_equal(oracle_lib.tb_from_t2(t2, 1, 8, 64), p)
+    for defect in range(5):
+        bad = p.copy()
+        if defect == 0:
+            bad[12] |= 1
+        elif defect == 1:
+            bad[5] = 1
+        else:
+            bad[0:4] = np.frombuffer(np.float32([-0.0, np.nan, 0.0][defect - 2]).tobytes(), np.uint8)
+        assert oracle_lib.tb_validate(bad, 1, 8, 64) == oracle_lib.ERR_ARGUMENT, defect
+
+
+@pytest.mark.parametrize("bs", [64, 128, 256])
+def test_bitplane_round_trip_and_scalar_parity(oracle_lib, bs):
+    """TernaryBitplaneTests.CorpusRoundTripPreservesEveryByteAndScalarResult: Ternary2 -> bitplane -> Ternary2
+    is byte-identical; the bitplane scalar MatVec equals the Ternary2 scalar MatVec; the bitplane AVX2 kernel
+    equals the Ternary2 AVX2 kernel (same logical codes, same lane arithmetic)."""
+    for name, rows, cols, w, x in list(critical_cases(bs)) + [numerical_random(3, c) for c in (1, 17, 257, 1000)]:
+        t2 = oracle_lib.t2_quantize(w, rows, cols, bs)
+        tb = oracle_lib.tb_from_t2(t2, rows, cols, bs)
+        assert oracle_lib.tb_validate(tb, rows, cols, bs) == oracle_lib.OK
+        assert np.array_equal(oracle_lib.tb_to_t2(tb, rows, cols, bs), t2), name
+        assert bits_equal(oracle_lib.tb_matvec(tb, rows, cols, bs, x, "scalar"),
+                          oracle_lib.t2_matvec(t2, rows, cols, bs, x, "scalar")), name
+        assert bits_equal(oracle_lib.tb_matvec(tb, rows, cols, bs, x, "avx2"),
+                          oracle_lib.t2_matvec(t2, rows, cols, bs, x, "avx2")), name
