@@ -259,6 +259,9 @@ __global__ void kq_float_kernel(const uint8_t *payload, int rows, int cols, cons
     for (int blk = 0; blk < nb; ++blk) {
         const uint8_t *b = payload + ((size_t)row * nb + blk) * BB;
         const float *xb = x + blk * 256;
+        // ExecuteScalar adds each block's DotBlock, which sums its own groups from zero; the execute order
+        // adds every group's horizontal sum straight into the row total.
+        float block_total = 0.0f;
         if (FMT == SATORI_Q4_K) {
             const float d = h2f(b), dmin = h2f(b + 2);
             for (int g = 0; g < 4; ++g) {
@@ -275,7 +278,7 @@ __global__ void kq_float_kernel(const uint8_t *payload, int rows, int cols, cons
                         lo = fadd(lo, fmul(__fsub_rn(fmul(dl, (float)(q[l] & 0xF)), ml), xb[g * 64 + l]));
                         hi = fadd(hi, fmul(__fsub_rn(fmul(dh, (float)(q[l] >> 4)), mh), xb[g * 64 + 32 + l]));
                     }
-                    total = fadd(total, fadd(lo, hi));
+                    block_total = fadd(block_total, fadd(lo, hi));
                 } else {
                     // QuantizedKAvx2Kernel.ExecuteQ4K (QuantizedKAvx2Kernel.cs:225-269).
                     float acc[8];
@@ -299,9 +302,9 @@ __global__ void kq_float_kernel(const uint8_t *payload, int rows, int cols, cons
                     for (int l = 0; l < 32; ++l) {
                         const int sub = l / 16;
                         for (int k = 0; k < 4; ++k)
-                            total = fadd(total, fmul(fmul(fmul(d, (float)scales[half * 8 + sub + 2 * k]),
-                                                          (float)q6k_code(b, half, l, k)),
-                                                     xb[half * 128 + l + 32 * k]));
+                            block_total = fadd(block_total, fmul(fmul(fmul(d, (float)scales[half * 8 + sub + 2 * k]),
+                                                                      (float)q6k_code(b, half, l, k)),
+                                                                 xb[half * 128 + l + 32 * k]));
                     }
                 } else {
                     // QuantizedKAvx2Kernel.ExecuteQ6K (QuantizedKAvx2Kernel.cs:271-316).
@@ -320,6 +323,7 @@ __global__ void kq_float_kernel(const uint8_t *payload, int rows, int cols, cons
                 }
             }
         }
+        if (!EXECUTE) total = fadd(total, block_total);
     }
     y[row] = total;
 }
