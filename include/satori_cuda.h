@@ -62,7 +62,12 @@ typedef enum satori_order {
     /* QuantizedMatVec.ExecuteScalar (:45-78); Ternary2MatVec.ExecuteScalar (Ternary2MatVec.cs:38-42). */
     SATORI_ORDER_SCALAR = 1,
     /* QuantizedMatVec.ExecuteBatch -> ExecuteBatchFloat/Dot with FMA (:104-120, 221-365): the decode path. */
-    SATORI_ORDER_BATCH = 2
+    SATORI_ORDER_BATCH = 2,
+    /* ExecuteBatch's result for a prefill chunk on the tensor cores (Q8_0 / Q4_0, cols % 64 == 0, any number
+       of positions): NOT bit-exact.  Weights and activations are split exactly into bf16 parts, every product
+       is exact, and the sum is accumulated in FP32 in tensor memory, so |y - y_ref| stays within a few FP32
+       roundings of sum|w*x| (the prefill tests bound it at 2e-6 of sum|w*x| + 1e-30). */
+    SATORI_ORDER_TENSOR = 3
 } satori_order;
 
 typedef struct satori_ctx satori_ctx;
@@ -107,6 +112,8 @@ SATORI_API int satori_matrix_execute_scalar(satori_matrix *m, const float *x, fl
 /* QuantizedMatVec.ExecuteBatch / GgufQuantizedMatrix.ExecuteBatch (GgufQuantizedMatrix.cs:43-48):
  * x[positions][cols] -> y[positions][rows], position-major, host pointers. Q8_0/Q4_0 only. */
 SATORI_API int satori_matrix_execute_batch(satori_matrix *m, const float *x, int positions, float *y);
+/* The same product in SATORI_ORDER_TENSOR (host x[positions][cols], y[positions][rows]). */
+SATORI_API int satori_matrix_execute_tensor(satori_matrix *m, const float *x, int positions, float *y);
 /* Device-pointer form of all three on the context stream (asynchronous). */
 SATORI_API int satori_matrix_execute_device(satori_matrix *m, const float *dx, float *dy, int positions, int order);
 /* GgufQuantizedMatrix.ReadRow (GgufQuantizedMatrix.cs:54-61): decodes one row to host memory,
@@ -212,6 +219,14 @@ SATORI_API int satori_session_append(satori_session *s, int token, float *logits
  * position's logits/argmax. */
 SATORI_API int satori_session_append_tokens(satori_session *s, const int *tokens, int count, float *logits,
                                             int *argmax);
+/* DenseSession.Forward (DenseSession.cs:136-181) with the prefill on the tensor cores: all tokens but the
+ * last run in chunks of up to 128 positions through DenseForward.LayerBatch's phases (DenseForward.cs:178-262),
+ * each projection one tcgen05 GEMM (SATORI_ORDER_TENSOR, so the cache rows match the per-token path to FP32
+ * rounding, not bit for bit); the last token runs through the decode step and yields logits/argmax as in
+ * satori_session_append_tokens.  Sharded sessions, one token, and weights other than Q8_0 / Q4_0 with
+ * multiples of 64 columns take the per-token path unchanged. */
+SATORI_API int satori_session_forward_tensor(satori_session *s, const int *tokens, int count, float *logits,
+                                             int *argmax);
 /* Greedy generation: appends `first`, then feeds back the argmax `count - 1` more times; writes the
  * `count` greedy tokens (TextGenerator.GenerateFromTokens' decode loop, TextGenerator.cs:62-99). */
 SATORI_API int satori_session_generate(satori_session *s, int first, int count, int *tokens_out);

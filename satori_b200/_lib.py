@@ -25,7 +25,7 @@ ERR_OUT_OF_MEMORY = 8
 Q8_0, Q4_0, T2_64, T2_128, T2_256 = 0, 1, 64, 128, 256
 Q4_K, Q6_K = 12, 14
 TB_64, TB_128, TB_256 = 1064, 1128, 1256
-ORDER_EXECUTE, ORDER_SCALAR, ORDER_BATCH = 0, 1, 2
+ORDER_EXECUTE, ORDER_SCALAR, ORDER_BATCH, ORDER_TENSOR = 0, 1, 2, 3
 
 
 class SatoriError(RuntimeError):
@@ -98,6 +98,7 @@ _SIGS = {
     "satori_matrix_execute": (C.c_int, [_vp, _vp, _vp]),
     "satori_matrix_execute_scalar": (C.c_int, [_vp, _vp, _vp]),
     "satori_matrix_execute_batch": (C.c_int, [_vp, _vp, C.c_int, _vp]),
+    "satori_matrix_execute_tensor": (C.c_int, [_vp, _vp, C.c_int, _vp]),
     "satori_matrix_execute_device": (C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int]),
     "satori_matrix_read_row": (C.c_int, [_vp, C.c_int, _vp]),
     "satori_matrix_info": (C.c_int, [_vp, _i32p, _i32p, _i32p, C.POINTER(C.c_size_t)]),
@@ -118,6 +119,7 @@ _SIGS = {
     "satori_nccl_unique_id": (C.c_int, [_vp]),
     "satori_session_append": (C.c_int, [_vp, C.c_int, _vp, _i32p]),
     "satori_session_append_tokens": (C.c_int, [_vp, _vp, C.c_int, _vp, _i32p]),
+"satori_session_forward_tensor": (C.c_int, [_vp, _vp, C.c_int, _vp, _i32p]),
     "satori_session_generate": (C.c_int, [_vp, C.c_int, C.c_int, _vp]),
     "satori_session_position": (C.c_int, [_vp, _i32p]),
     "satori_session_reset": (C.c_int, [_vp]),

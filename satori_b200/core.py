@@ -214,6 +214,16 @@ class CudaQuantizedMatrix:
         check(_lib.lib().satori_matrix_execute_batch(self.handle, _ptr(x), positions, _ptr(y)), "execute_batch")
         return _commit(y, output)
 
+    def execute_tensor(self, input, positions: int, output: np.ndarray | None = None) -> np.ndarray:
+        """ExecuteBatch's product on the tensor cores (Q8_0 / Q4_0): exact products, FP32 accumulation in
+        tensor memory -- not the reference's operation order, within a few FP32 roundings of it."""
+        if positions <= 0:
+            raise ArgumentError(_lib.ERR_ARGUMENT, "positions must be positive")
+        x = _f32(input, positions * self.columns, "input")
+        y = np.empty(positions * self.rows, np.float32)
+        check(_lib.lib().satori_matrix_execute_tensor(self.handle, _ptr(x), positions, _ptr(y)), "execute_tensor")
+        return _commit(y, output)
+
     def execute_device(self, dx: int, dy: int, positions: int = 1, order: int = _lib.ORDER_BATCH) -> None:
         check(_lib.lib().satori_matrix_execute_device(self.handle, dx, dy, positions, order), "execute_device")
 

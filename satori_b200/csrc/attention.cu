@@ -41,7 +41,24 @@ struct AttnParams {
     float *out;
     unsigned *err;
     int use_pdl;
+    // Prefill chunk: position z of the batch (blockIdx.z of the partial kernels, blockIdx.y of the merge)
+    // reads q + z * q_pstride, attends to tokens + z tokens and writes out + z * out_pstride.
+    int batch;
+    long long q_pstride, out_pstride;
 };
+
+// The parameters of batch position z.
+__device__ __forceinline__ AttnParams attn_at(const AttnParams &in, int z)
+{
+    AttnParams p = in;
+    if (z > 0) {
+        p.q += z * in.q_pstride;
+        p.out += z * in.out_pstride;
+        p.scratch += (long long)z * in.nsplit * in.q_heads * (in.head_dim + 2);
+        p.tokens += z;
+    }
+    return p;
+}
 
 // Sum across the warp of N values per lane, N a power of two <= 8.  On return v[0] holds, in
 // every lane, the total of head (lane / (32 / N)); all lanes of a head hold identical bits.
@@ -83,8 +100,9 @@ template <int DPL, bool VEC4>
 __device__ __forceinline__ int dim_of(int lane, int i) { return VEC4 ? 4 * lane + i : lane + 32 * i; }
 
 template <int DPL, bool VEC4, int GMAX>
-__global__ void __launch_bounds__(kWarps * 32) attn_partial_kernel(AttnParams p)
+__global__ void __launch_bounds__(kWarps * 32) attn_partial_kernel(const AttnParams pin)
 {
+    const AttnParams p = attn_at(pin, blockIdx.z);
     constexpr int R = 32 / GMAX;  // lanes per head after the transposed reduction
     __shared__ float P[kWarps][GMAX][kTokBlock];
     __shared__ float wm[kWarps][GMAX], wl[kWarps][GMAX];
@@ -313,8 +331,10 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const void *map, int c0, 
 }
 
 __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
-    attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnParams p)
+    attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                       const AttnParams pin)
 {
+    const AttnParams p = attn_at(pin, blockIdx.z);
     constexpr int GMAX = 8, DPL = 4, R = 32 / GMAX;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
@@ -523,8 +543,9 @@ __device__ __forceinline__ void cp_async4(float *dst, const float *src)
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
-__global__ void __launch_bounds__(kMergeThreads) attn_merge_kernel(AttnParams p)
+__global__ void __launch_bounds__(kMergeThreads) attn_merge_kernel(const AttnParams pin)
 {
+    const AttnParams p = attn_at(pin, blockIdx.y);
     extern __shared__ float msm[];   // wts[nsplit] (padded to 4), then chunk[kMergeChunk][head_dim + 2]
     __shared__ float wmax[kMergeThreads / 32];
     __shared__ double sbuf[128];
@@ -631,9 +652,17 @@ __global__ void rope_append_kernel(RopeAppendArgs a)
         pdl_launch_dependents();
         pdl_wait();
     }
-    const int pos = a.position_dev ? *a.position_dev : a.position;
+    const int z = blockIdx.y;
+    const int pos = (a.position_dev ? *a.position_dev : a.position) + z;
     const int hd = a.head_dim, half = a.rotary / 2;
     const int qw = a.q_heads * hd, kvw = a.kv_heads * hd;
+    if (z > 0) {
+        a.q += z * a.in_stride;
+        a.k += z * a.in_stride;
+        a.v += z * a.in_stride;
+        a.q_out += (long long)z * qw;
+        if (a.table) a.table += (long long)z * a.rotary;
+    }
     float *kslot = a.k_cache + (long long)pos * kvw;
     float *vslot = a.v_cache + (long long)pos * kvw;
     // TransformerOps.RopeHalf (TransformerOps.cs:99-118): FP64 angle and rotation, FP32 result.
@@ -686,21 +715,22 @@ __global__ void rope_half_kernel(float *v, int n, int hd, int pos, double base, 
 
 }  // namespace
 
-int attn_splits(int q_heads, int kv_heads, int head_dim, int max_tokens, int sm_count)
+int attn_splits(int q_heads, int kv_heads, int head_dim, int max_tokens, int sm_count, int batch)
 {
     const int group = q_heads / kv_heads;
     const int gmax = gmax_for(group);
     const int ngroups = (group + gmax - 1) / gmax;
-    const int units = kv_heads * ngroups;
+    const int units = kv_heads * ngroups * std::max(1, batch);
     int nsplit = std::max(1, (3 * sm_count + units - 1) / units);
     nsplit = std::min(nsplit, std::max(1, max_tokens / (2 * kTokBlock)));
     (void)head_dim;
     return nsplit;
 }
 
-size_t attn_scratch_floats(int q_heads, int kv_heads, int head_dim, int max_tokens, int sm_count)
+size_t attn_scratch_floats(int q_heads, int kv_heads, int head_dim, int max_tokens, int sm_count, int batch)
 {
-    return (size_t)attn_splits(q_heads, kv_heads, head_dim, max_tokens, sm_count) * q_heads * (head_dim + 2);
+    return (size_t)attn_splits(q_heads, kv_heads, head_dim, max_tokens, sm_count, batch) * q_heads *
+           (head_dim + 2) * std::max(1, batch);
 }
 
 namespace {
@@ -742,20 +772,20 @@ bool launch_stream(const AttnArgs &a, AttnParams &p, int gmax, int sm_count, cud
 {
     if (a.head_dim != 128 || gmax != 8) return false;
     const int units = a.kv_heads * p.ngroups;
-    const int cap = std::max(a.max_tokens, a.tokens);
+    const int cap = std::max(a.max_tokens, a.tokens + p.batch - 1);
     CUtensorMap kmap, vmap;
     if (!encode_kv_map(&kmap, a.keys, a.kv_heads, p.kv_stride, cap) ||
         !encode_kv_map(&vmap, a.values, a.kv_heads, p.kv_stride, cap))
         return false;
     // About one CTA per SM (each keeps ~64 KB in flight); never more splits than the scratch holds.
-    p.nsplit = std::max(1, std::min(p.nsplit, (sm_count + units - 1) / units));
+    p.nsplit = std::max(1, std::min(p.nsplit, (sm_count + units * p.batch - 1) / (units * p.batch)));
     const cudaError_t e = opt_in_smem(reinterpret_cast<const void *>(attn_stream_kernel), kStreamSmem);
     if (e != cudaSuccess) {
         *err = e;
         return true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.nsplit, units);
+    cfg.gridDim = dim3(p.nsplit, units, p.batch);
     cfg.blockDim = dim3((kStreamWarps + 1) * 32);
     cfg.dynamicSmemBytes = kStreamSmem;
     cfg.stream = stream;
@@ -772,6 +802,8 @@ bool launch_stream(const AttnArgs &a, AttnParams &p, int gmax, int sm_count, cud
 cudaError_t launch_attention(const AttnArgs &a, int sm_count, cudaStream_t stream)
 {
     if (a.head_dim <= 0 || a.head_dim > 256 || a.q_heads % a.kv_heads != 0) return cudaErrorInvalidValue;
+    const int batch = std::max(1, a.batch);
+    if (batch > 1 && (a.tokens_dev || a.tokens < 1 || batch > 65535)) return cudaErrorInvalidValue;
     AttnParams p;
     p.q = a.q;
     p.keys = a.keys;
@@ -785,7 +817,10 @@ cudaError_t launch_attention(const AttnArgs &a, int sm_count, cudaStream_t strea
     p.ngroups = (p.group + gmax - 1) / gmax;
     p.tokens = a.tokens;
     p.tokens_dev = a.tokens_dev;
-    p.nsplit = attn_splits(a.q_heads, a.kv_heads, a.head_dim, a.max_tokens, sm_count);
+    p.nsplit = attn_splits(a.q_heads, a.kv_heads, a.head_dim, a.max_tokens, sm_count, batch);
+    p.batch = batch;
+    p.q_pstride = a.q_pstride;
+    p.out_pstride = a.out_pstride;
     p.scale = (float)(1.0 / std::sqrt((double)a.head_dim));
     p.scratch = a.scratch;
     p.out = a.out;
@@ -793,13 +828,13 @@ cudaError_t launch_attention(const AttnArgs &a, int sm_count, cudaStream_t strea
     p.err = a.err;
     cudaError_t e;
     if (!launch_stream(a, p, gmax, sm_count, stream, &e)) {
-        const dim3 grid(p.nsplit, a.kv_heads * p.ngroups);
+        const dim3 grid(p.nsplit, a.kv_heads * p.ngroups, batch);
         if (a.head_dim == 128) e = launch_partial_g<4, true>(p, gmax, grid, stream);
         else e = launch_partial_g<8, false>(p, gmax, grid, stream);
     }
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.q_heads);
+    cfg.gridDim = dim3(a.q_heads, batch);
     cfg.blockDim = dim3(kMergeThreads);
     cfg.dynamicSmemBytes = sizeof(float) * ((size_t)((p.nsplit + 3) & ~3) + (size_t)kMergeChunk * (a.head_dim + 2));
     const cudaError_t ea = opt_in_smem(reinterpret_cast<const void *>(attn_merge_kernel), cfg.dynamicSmemBytes);
@@ -816,8 +851,10 @@ cudaError_t launch_attention(const AttnArgs &a, int sm_count, cudaStream_t strea
 cudaError_t launch_rope_append(const RopeAppendArgs &a, cudaStream_t stream)
 {
     const int n = (a.q_heads + 2 * a.kv_heads) * a.head_dim;
+    const int batch = std::max(1, a.batch);
+    if (batch > 1 && (a.position_dev || batch > 65535)) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.table ? (n + 255) / 256 : 1);
+    cfg.gridDim = dim3(a.table ? (n + 255) / 256 : 1, batch);
     cfg.blockDim = dim3(a.table ? 256 : 512);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

@@ -19,12 +19,17 @@ struct AttnArgs {
     float *scratch;       // partial records, attn_scratch_floats() floats
     unsigned *err;
     int use_pdl;
+    // Prefill chunk of `batch` positions (0 or 1: one position): position z reads q + z * q_pstride,
+    // attends to the first tokens + z tokens (the causal prefix; tokens_dev must be null) and writes
+    // out + z * out_pstride.
+    int batch;
+    long long q_pstride, out_pstride;
 };
 
 // Number of split-K work units (CTAs along the sequence) for a given shape.
-int attn_splits(int q_heads, int kv_heads, int head_dim, int max_tokens, int sm_count);
-// Scratch the partial records need: splits * q_heads * (head_dim + 2) floats.
-size_t attn_scratch_floats(int q_heads, int kv_heads, int head_dim, int max_tokens, int sm_count);
+int attn_splits(int q_heads, int kv_heads, int head_dim, int max_tokens, int sm_count, int batch = 1);
+// Scratch the partial records need: batch * splits * q_heads * (head_dim + 2) floats.
+size_t attn_scratch_floats(int q_heads, int kv_heads, int head_dim, int max_tokens, int sm_count, int batch = 1);
 cudaError_t launch_attention(const AttnArgs &a, int sm_count, cudaStream_t stream);
 
 // RopeHalf on q and k at `position`, then append k and v at slot `position` of the cache; the
@@ -39,6 +44,11 @@ struct RopeAppendArgs {
     const int *position_dev;
     const double *table;        // optional [rotary/2][cos, sin] for this position (launch_embed writes it)
     int use_pdl;
+    // Prefill chunk of `batch` positions (0 or 1: one): position z = position + z reads q/k/v + z * in_stride,
+    // writes q_out + z * q_heads * head_dim and its cache slot, and takes table + z * rotary when a table
+    // is given.  position_dev must be null.
+    int batch;
+    long long in_stride;
 };
 cudaError_t launch_rope_append(const RopeAppendArgs &a, cudaStream_t stream);
 

@@ -165,6 +165,37 @@ int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int 
     const size_t hint_bytes = hint ? ctx->next_bytes : 0;
     ctx->next_payload = nullptr;
     ctx->next_bytes = 0;
+    if (order == SATORI_ORDER_TENSOR) {
+        if (norm_w || xp || xw)
+            return set_error(SATORI_ERR_NOT_SUPPORTED, "the tensor order takes no fused RmsNorm or exchange");
+        if (!tc_gemm_takes(rows, cols, format, 1, epilogue))
+            return set_error(SATORI_ERR_NOT_SUPPORTED,
+                             "the tensor order takes Q8_0 / Q4_0 with a multiple of 64 columns");
+        for (int p0 = 0; p0 < positions; p0 += 128) {
+            const int np = std::min(128, positions - p0);
+            const size_t need = tc_scratch_bytes(rows, cols, np, ctx->sm_count);
+            int rc = ensure_tc_scratch(ctx, need);
+            if (rc) return rc;
+            TcGemm g = {};
+            g.payload = d_payload;
+            g.rows = rows;
+            g.cols = cols;
+            g.format = format;
+            g.x = dx + (size_t)p0 * cols;
+            g.positions = np;
+            g.epilogue = epilogue;
+            const int ldy = epilogue == kEpiSwiGlu ? rows / 2 : rows;
+            g.y = dy ? dy + (size_t)p0 * ldy : nullptr;
+            g.bias = bias;
+            g.residual = residual ? residual + (size_t)p0 * rows : nullptr;
+            g.scratch = ctx->tc_scratch;
+            g.scratch_bytes = ctx->tc_scratch_bytes;
+            g.err = ctx->d_err;
+            cudaError_t e = launch_tc_gemm(g, ctx->sm_count, stream);
+            if (e != cudaSuccess) return cuda_fail(e, "launch tensor-core projection");
+        }
+        return SATORI_OK;
+    }
     if (is_kquant(format)) {
         if (norm_w || xp || xw || epilogue == kEpiSwiGlu)
             return set_error(SATORI_ERR_NOT_SUPPORTED, "fused RmsNorm / SwiGLU / exchange are not available for K-quants");
@@ -353,6 +384,7 @@ extern "C" int satori_destroy(satori_ctx *ctx)
     cudaFree(ctx->d_err);
     cudaFree(ctx->d_status);
     cudaFree(ctx->attn_scratch);
+    cudaFree(ctx->tc_scratch);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return SATORI_OK;
@@ -468,12 +500,21 @@ extern "C" int satori_matrix_execute_batch(satori_matrix *m, const float *x, int
     return matrix_execute_host(m, x, y, positions, SATORI_ORDER_BATCH);
 }
 
+extern "C" int satori_matrix_execute_tensor(satori_matrix *m, const float *x, int positions, float *y)
+{
+    if (m && m->format != SATORI_Q8_0 && m->format != SATORI_Q4_0)
+        return set_error(SATORI_ERR_NOT_SUPPORTED, "the tensor order is defined for Q8_0 / Q4_0");
+    return matrix_execute_host(m, x, y, positions, SATORI_ORDER_TENSOR);
+}
+
 extern "C" int satori_matrix_execute_device(satori_matrix *m, const float *dx, float *dy, int positions, int order)
 {
     if (!m) return set_error(SATORI_ERR_DISPOSED, "matrix is disposed");
     if (!dx || !dy || positions <= 0) return set_error(SATORI_ERR_ARGUMENT, "bad device vectors/positions");
-    if (order < 0 || order > 2) return set_error(SATORI_ERR_ARGUMENT, "bad order %d", order);
-    if (order != SATORI_ORDER_BATCH && positions != 1)
+    if (order < 0 || order > 3) return set_error(SATORI_ERR_ARGUMENT, "bad order %d", order);
+    if (order == SATORI_ORDER_TENSOR && m->format != SATORI_Q8_0 && m->format != SATORI_Q4_0)
+        return set_error(SATORI_ERR_NOT_SUPPORTED, "the tensor order is defined for Q8_0 / Q4_0");
+    if (order < SATORI_ORDER_BATCH && positions != 1)
         return set_error(SATORI_ERR_ARGUMENT, "only the batch order takes several positions");
     if (order == SATORI_ORDER_BATCH && m->format >= 64)
         return set_error(SATORI_ERR_NOT_SUPPORTED, "ExecuteBatch is defined for the GGUF formats only");
@@ -573,6 +614,21 @@ static int attention_args_ok(int q_heads, int kv_heads, int head_dim, int tokens
     if (head_dim <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads != 0 || tokens <= 0)
         return set_error(SATORI_ERR_ARGUMENT, "Invalid grouped-attention dimensions.");
     if (head_dim > 256) return set_error(SATORI_ERR_NOT_SUPPORTED, "head_dim > 256 is not supported");
+    return SATORI_OK;
+}
+
+int satori::ensure_tc_scratch(satori_ctx *ctx, size_t bytes)
+{
+    if (bytes <= ctx->tc_scratch_bytes) return SATORI_OK;
+    // Earlier launches on the stream may still read the old buffer.
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "synchronise before growing scratch");
+    cudaFree(ctx->tc_scratch);
+    ctx->tc_scratch = nullptr;
+    ctx->tc_scratch_bytes = 0;
+    e = cudaMalloc(&ctx->tc_scratch, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "allocate tensor-order scratch");
+    ctx->tc_scratch_bytes = bytes;
     return SATORI_OK;
 }
 

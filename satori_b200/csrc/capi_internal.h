@@ -24,6 +24,8 @@ struct satori_ctx {
     // head into L2 during its tail.  Set by the caller just before run_gemv, consumed (cleared) by it.
     const uint8_t *next_payload = nullptr;
     size_t next_bytes = 0;
+    uint8_t *tc_scratch = nullptr;     // grow-only split activations + split-K tiles of tensor-order calls
+    size_t tc_scratch_bytes = 0;
 };
 
 struct satori_matrix {
@@ -50,6 +52,8 @@ int validate_shape(int rows, int cols, int format);
 // Uploads and validates a payload; on success *out owns a device copy padded for bulk copies.
 int upload_payload(satori_ctx *ctx, const uint8_t *src, bool src_is_device, size_t bytes, int rows, int cols,
                    int format, uint8_t **out);
+// Grows the context's tensor-order scratch to at least `bytes`.
+int ensure_tc_scratch(satori_ctx *ctx, size_t bytes);
 // Runs the MatVec on device pointers with the library's plan for this shape.
 int run_gemv(satori_ctx *ctx, const uint8_t *d_payload, int rows, int cols, int format, int order,
              const float *dx, float *dy, int positions, int epilogue, const float *bias, float *residual,

@@ -89,6 +89,26 @@ cudaError_t launch_bitplane_decode_row(const uint8_t *payload, int cols, int for
                                        int row_host, float *out, cudaStream_t stream);
 cudaError_t launch_bitplane_validate(const uint8_t *payload, int rows, int cols, int format, int *status_dev,
                                      cudaStream_t stream);
+// prefill_gemm.cu: the projection of a chunk of up to 128 positions on the tensor cores (Q8_0 / Q4_0,
+// cols % 64 == 0).  Not the reference's FP32 order: exact products, FP32 accumulation in tensor memory.
+struct TcGemm {
+    const uint8_t *payload;
+    int rows, cols, format;
+    const float *x;          // [positions][cols]
+    int positions;
+    int epilogue;            // kEpiNone / kEpiBias / kEpiResidual / kEpiSwiGlu
+    float *y;                // y[p * ldy + r] (SwiGlu: y[p * ldy + r / 2]); unused by kEpiResidual when null
+    int ldy;                 // 0: rows (SwiGlu: rows / 2)
+    const float *bias;
+    float *residual;         // residual[p * ldr + r] += acc
+    int ldr;                 // 0: rows
+    uint8_t *scratch;        // tc_scratch_bytes(); 256-byte aligned
+    size_t scratch_bytes;
+    unsigned *err;
+};
+bool tc_gemm_takes(int rows, int cols, int format, int positions, int epilogue);
+size_t tc_scratch_bytes(int rows, int cols, int positions, int sm_count);
+cudaError_t launch_tc_gemm(const TcGemm &g, int sm_count, cudaStream_t stream);
 int gemv_block_bytes(int format);
 int gemv_block_elems(int format);
 

@@ -46,20 +46,22 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const floa
         pdl_launch_dependents();
         pdl_wait();
     }
+    x += (long long)blockIdx.x * n;     // one vector per CTA (a prefill chunk has several)
+    out += (long long)blockIdx.x * n;
     rms_partial(x, n, threadIdx.x, red);
     __syncthreads();
     const double scale = rms_scale(red, n, eps);
     for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = rms_apply(x[i], scale, w[i]);
 }
 
-__global__ void rmsnorm_heads_kernel(float *v, int n, const float *w, float eps, int hd, int pdl)
+__global__ void rmsnorm_heads_kernel(float *v, int n, const float *w, float eps, int hd, long long stride, int pdl)
 {
     __shared__ double red[128];
     if (pdl) {
         pdl_launch_dependents();
         pdl_wait();
     }
-    float *h = v + (long long)blockIdx.x * hd;
+    float *h = v + (long long)blockIdx.y * stride + (long long)blockIdx.x * hd;
     double sum = 0;
     for (int i = threadIdx.x; i < hd; i += blockDim.x) sum = __dadd_rn(sum, __dmul_rn((double)h[i], (double)h[i]));
     sum = block_sum_double(sum, red);
@@ -107,6 +109,33 @@ __global__ void embed_kernel(const uint8_t *embd, int cols, const int *token_dev
         hidden[i] = fmul(d, code);  // QuantizedRow.DecodeQ8Block
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) *tokens_dev = *pos_dev + 1;
+}
+
+// A prefill chunk's embedding rows (token of position z from tokens[z]) and RoPE factors of positions
+// pos0 + z, z = blockIdx.y: the per-position work of embed_kernel.
+__global__ void embed_batch_kernel(const uint8_t *embd, int cols, const int *tokens, int pos0, float *hidden,
+                                   double *rope_table, double rope_base, int rotary)
+{
+    const int z = blockIdx.y;
+    if (rope_table) {
+        const int k = blockIdx.x * blockDim.x + threadIdx.x;
+        if (k < rotary / 2) {
+            const double angle = __ddiv_rn((double)(pos0 + z), pow(rope_base, __ddiv_rn(2.0 * k, (double)rotary)));
+            double sn, cs;
+            sincos(angle, &sn, &cs);
+            rope_table[(long long)z * rotary + 2 * k] = cs;
+            rope_table[(long long)z * rotary + 2 * k + 1] = sn;
+        }
+    }
+    const int bpr = cols / 32;
+    const uint8_t *row = embd + (long long)tokens[z] * bpr * 34;
+    float *out = hidden + (long long)z * cols;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < cols; i += gridDim.x * blockDim.x) {
+        const uint8_t *blk = row + (i / 32) * 34;
+        const float d = half_bits_to_float((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
+        const float code = u8_to_f_minus((uint32_t)blk[2 + (i & 31)] ^ 0x80u, 128.0f);
+        out[i] = fmul(d, code);
+    }
 }
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, int idx)
@@ -170,7 +199,29 @@ cudaError_t launch_rmsnorm(const float *x, const float *w, int n, float eps, flo
 
 cudaError_t launch_rmsnorm_heads(float *v, int n, const float *w, float eps, int head_dim, cudaStream_t s, int pdl)
 {
-    return launch_ex(rmsnorm_heads_kernel, dim3(n / head_dim), dim3(128), 0, s, pdl, v, n, w, eps, head_dim, pdl);
+    return launch_ex(rmsnorm_heads_kernel, dim3(n / head_dim), dim3(128), 0, s, pdl, v, n, w, eps, head_dim, 0ll,
+                     pdl);
+}
+
+cudaError_t launch_rmsnorm_batch(const float *x, const float *w, int n, float eps, float *out, int positions,
+                                 cudaStream_t s)
+{
+    return launch_ex(rmsnorm_kernel, dim3(positions), dim3(256), 0, s, 0, x, w, n, eps, out, 0);
+}
+
+cudaError_t launch_rmsnorm_heads_batch(float *v, int n, const float *w, float eps, int head_dim, long long stride,
+                                       int positions, cudaStream_t s)
+{
+    return launch_ex(rmsnorm_heads_kernel, dim3(n / head_dim, positions), dim3(128), 0, s, 0, v, n, w, eps, head_dim,
+                     stride, 0);
+}
+
+cudaError_t launch_embed_batch(const uint8_t *embd, int cols, const int *tokens_dev, int positions, int pos0,
+                               float *hidden, double *rope_table, double rope_base, int rotary, cudaStream_t s)
+{
+    const int blocks = (std::max(cols, rotary / 2) + 255) / 256;
+    return launch_ex(embed_batch_kernel, dim3(blocks, positions), dim3(256), 0, s, 0, embd, cols, tokens_dev, pos0,
+                     hidden, rope_table, rope_base, rotary);
 }
 
 cudaError_t launch_swiglu(const float *gate, const float *up, int n, float *out, cudaStream_t s, int pdl)

@@ -19,6 +19,16 @@ cudaError_t launch_swiglu(const float *gate, const float *up, int n, float *out,
 // position *pos_dev, k < rotary/2) for every layer's rope_append to read.
 cudaError_t launch_embed(const uint8_t *embd, int cols, const int *token_dev, const int *pos_dev, int *tokens_dev,
                          float *hidden, double *rope_table, double rope_base, int rotary, cudaStream_t s, int pdl);
+// Prefill chunk forms (`positions` vectors, one after another unless a stride is given; no PDL):
+// RmsNorm of each position's vector, RmsNormHeads of each position's heads (vectors `stride` floats
+// apart), and the embedding rows of tokens_dev[0..positions) with the RoPE factors of positions
+// pos0 .. pos0 + positions - 1 ([positions][rotary/2][cos, sin]).
+cudaError_t launch_rmsnorm_batch(const float *x, const float *w, int n, float eps, float *out, int positions,
+                                 cudaStream_t s);
+cudaError_t launch_rmsnorm_heads_batch(float *v, int n, const float *w, float eps, int head_dim, long long stride,
+                                       int positions, cudaStream_t s);
+cudaError_t launch_embed_batch(const uint8_t *embd, int cols, const int *tokens_dev, int positions, int pos0,
+                               float *hidden, double *rope_table, double rope_base, int rotary, cudaStream_t s);
 // GreedyTokenSelector.Select (src/Satori.Core/GreedyTokenSelector.cs:6-16): smallest index of the
 // maximum; a non-finite logit sets *nonfinite_dev.  Then advances *pos_dev and feeds *token_dev.
 // `scratch` = 4 zeroed words (8-byte aligned) the launch leaves zeroed again.

@@ -528,6 +528,14 @@ int session_build(satori_session *s, const satori_model_desc *d, satori_session 
 
 int session_check_desc(const satori_model_desc *d, int context) { return check_desc(d, context); }
 
+int session_dalloc_bytes(satori_session *s, void **p, size_t bytes)
+{
+    uint8_t *b = nullptr;
+    TRY(dalloc(s, &b, bytes));
+    *p = b;
+    return SATORI_OK;
+}
+
 extern "C" int satori_session_create(satori_ctx *ctx, const satori_model_desc *d, int context, satori_session **out)
 {
     if (!ctx || !out) return set_error(SATORI_ERR_ARGUMENT, "null argument");

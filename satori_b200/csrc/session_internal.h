@@ -87,12 +87,21 @@ struct satori_session {
 
     ShardState *shard = nullptr;
     bool failed = false;             // a peer stopped answering: every later step is refused
+
+    // Tensor-core prefill (session_prefill.cu): chunk buffers, allocated by the first such call.
+    int pf_ready = 0;                // 1 allocated, -1 the weights do not qualify
+    int *pf_tokens = nullptr;        // [context] tokens of the call
+    float *pf_hidden = nullptr, *pf_normed = nullptr, *pf_qkv = nullptr, *pf_qrot = nullptr, *pf_ctx = nullptr;
+    float *pf_act = nullptr, *pf_gate = nullptr, *pf_up = nullptr, *pf_attn = nullptr;
+    double *pf_rope = nullptr;       // [chunk][rotary/2][cos, sin]
 };
 
 satori_session *session_new(satori_ctx *ctx, const satori_model_desc *d, int context);
 int session_check_desc(const satori_model_desc *d, int context);
 int session_build(satori_session *s, const satori_model_desc *d, satori_session **out);
 int session_alloc_state(satori_session *s);
+// Device buffer owned by the session (freed with it), zeroed.
+int session_dalloc_bytes(satori_session *s, void **p, size_t bytes);
 void session_destroy_sharding(satori_session *s);
 // Fills the rank's ranges (world 1: everything).  Returns a satori_status.
 int session_plan_shards(satori_session *s);

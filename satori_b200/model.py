@@ -239,26 +239,29 @@ class CudaDenseSession:
                                                logits.ctypes.data if want_logits else None, C.byref(arg)), "append")
         return logits, arg.value
 
-    def forward(self, tokens, logits: np.ndarray | None = None) -> np.ndarray:
-        """IInferenceSession.Forward: appends every token, writes the last position's logits."""
+    def forward(self, tokens, logits: np.ndarray | None = None, tensor_cores: bool = False) -> np.ndarray:
+        """IInferenceSession.Forward: appends every token, writes the last position's logits.
+
+        tensor_cores=True prefills all but the last token in chunks on the tensor cores
+        (satori_session_forward_tensor): not bit-exact, within FP32 rounding of the per-token path."""
         t = np.ascontiguousarray(tokens, dtype=np.int32)
         if t.size == 0:
             raise ArgumentError(_lib.ERR_ARGUMENT, "At least one token is required.")
         out = np.empty(self.vocab, np.float32)
         arg = C.c_int()
-        check(_lib.lib().satori_session_append_tokens(self.handle, t.ctypes.data, t.size, out.ctypes.data,
-                                                      C.byref(arg)), "forward")
+        fn = _lib.lib().satori_session_forward_tensor if tensor_cores else _lib.lib().satori_session_append_tokens
+        check(fn(self.handle, t.ctypes.data, t.size, out.ctypes.data, C.byref(arg)), "forward")
         if logits is not None:
             logits[:] = out
             return logits
         return out
 
-    def prefill(self, tokens) -> int:
+    def prefill(self, tokens, tensor_cores: bool = False) -> int:
         """Appends every token without copying logits back; returns the last greedy token."""
         t = np.ascontiguousarray(tokens, dtype=np.int32)
         arg = C.c_int()
-        check(_lib.lib().satori_session_append_tokens(self.handle, t.ctypes.data, t.size, None, C.byref(arg)),
-              "prefill")
+        fn = _lib.lib().satori_session_forward_tensor if tensor_cores else _lib.lib().satori_session_append_tokens
+        check(fn(self.handle, t.ctypes.data, t.size, None, C.byref(arg)), "prefill")
         return arg.value
 
     def generate(self, first: int, count: int) -> np.ndarray:
