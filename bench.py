@@ -319,6 +319,87 @@ def kernel_ternary(ctx, stream, n, bs, order="execute", **kw):
     return nbytes, ms, copies
 
 
+PREFILL_SHAPES = [("qkv", 1, 4608, 3584), ("o", 1, 3584, 3584), ("gate_up", 1, 37888, 3584),
+                  ("down", 1, 3584, 18944), ("lm_head", 0, 152064, 3584)]
+
+
+def _tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
+
+
+def kernel_prefill_gemm(ctx, stream, name, fmt, rows, cols, positions=128, min_region_s=0.5, repeats=5):
+    """One 7B projection of a 128-position prefill chunk on the tensor cores (SATORI_ORDER_TENSOR: the
+    activation split, the tcgen05 GEMM and, for split-K shapes, the ordered reduction)."""
+    import torch
+
+    import satori_b200 as sat
+    from satori_b200 import _lib
+    dev = device_quantized(ctx, rows, cols, fmt, seed=5 + rows)
+    m = sat.CudaQuantizedMatrix.from_device(ctx, dev.data_ptr(), dev.numel(), rows, cols, fmt)
+    del dev
+    x = torch.randn(positions * cols, generator=torch.Generator(device="cuda").manual_seed(3), device="cuda")
+    y = torch.empty(positions * rows, device="cuda")
+    torch.cuda.synchronize()
+    ctx.set_stream(stream.cuda_stream)
+    with torch.cuda.stream(stream):      # grows the scratch before capture
+        m.execute_device(x.data_ptr(), y.data_ptr(), positions, _lib.ORDER_TENSOR)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        m.execute_device(x.data_ptr(), y.data_ptr(), positions, _lib.ORDER_TENSOR)
+    torch.cuda.synchronize()
+    ms = repeat_regions(graph.replay, stream, 1, min_region_s=min_region_s, repeats=repeats)
+    ctx.set_stream(None)
+    del graph
+    m.dispose()
+    best, med = min(ms), statistics.median(ms)
+    flops = 2.0 * rows * cols * positions
+    mmas = 6 if fmt == 0 else 5          # bf16 part products per weight/activation pair
+    peak, kind = _tensor_peak()
+    pipe = flops * mmas / (best / 1e3) / 1e12
+    return {"shape": f"{name} {rows}x{cols} {'Q8_0' if fmt == 0 else 'Q4_0'}, {positions} positions",
+            "us_min": round(best * 1e3, 2), "us_median": round(med * 1e3, 2),
+            "spread": round((max(ms) - best) / best, 4), "repeats": len(ms),
+            "logical_tflops": round(flops / (best / 1e3) / 1e12, 1),
+            "tensor_pipe_tflops": round(pipe, 1), "mma_parts_per_product": mmas,
+            "peak_tflops": peak, "peak_kind": kind, "frac": round(pipe / peak, 4),
+            "weight_gbs": round(rows * (cols // 32) * (34 if fmt == 0 else 18) / (best / 1e3) / GB, 1)}
+
+
+def prefill_record(sess, spec, P, stream_ctx, repeats=3):
+    """satori_session_forward_tensor on a P-token prompt from position 0 (reset before each run): the
+    tensor-core prefill of the first P - 1 tokens plus the last token's decode step, device time."""
+    import torch
+    prompt = np.random.default_rng(4).integers(0, spec.vocab, P).astype(np.int32)
+    ext = torch.cuda.ExternalStream(stream_ctx.stream)
+    sess.reset()
+    sess.forward(prompt, tensor_cores=True)      # allocates the chunk buffers
+    times = []
+    for _ in range(repeats):
+        sess.reset()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(ext)
+        t0 = time.perf_counter()
+        sess.forward(prompt, tensor_cores=True)
+        wall = time.perf_counter() - t0
+        end.record(ext)
+        torch.cuda.synchronize()
+        times.append((start.elapsed_time(end), wall))
+    best = min(t[0] for t in times)
+    best_wall = min(t[1] for t in times)
+    return {"prompt_tokens": P, "chunk_positions": 128, "ms_min": round(best, 2),
+            "tokens_per_s": round(P / (best / 1e3), 1), "e2e_tokens_per_s": round(P / best_wall, 1),
+            "repeats": repeats,
+            "api": "satori_session_forward_tensor (host tokens in, host logits out)",
+            "order": "projections on tcgen05, FP32 accumulation of exact bf16 part products (not bit-exact); "
+                     "the rest as the decode step"}
+
+
 def kernels_record(ctx, min_region_s=0.5, repeats=5):
     import torch
     peak, kind = _peaks()
@@ -338,6 +419,8 @@ def kernels_record(ctx, min_region_s=0.5, repeats=5):
         out[f"ternary2_4096x4096_bs{bs}"] = stats_record(b, ms, peak, kind,
                                                          {"workload": f"configs[0] bs{bs}", "copies": copies,
                                                           "order": "Ternary2Avx2Kernel, bit-exact"})
+    for name, fmt, rows, cols in PREFILL_SHAPES:
+        out[f"prefill_gemm_{name}"] = kernel_prefill_gemm(ctx, stream, name, fmt, rows, cols, **kw)
     return out
 
 
@@ -527,6 +610,8 @@ def bench_decode(args, rank, world, local, spec, with_kernels: bool):
         "first_tokens": [int(t) for t in ref_tokens[:8]],
         "clocks": clocks.summary(),
     }
+    if world == 1 and not args.no_prefill:
+        res["prefill"] = prefill_record(sess, spec, P, ctx)
     sess.dispose()
     if with_kernels and rank == 0 and world == 1:
         res["kernels"] = kernels_record(ctx)
@@ -550,6 +635,11 @@ def bench_kernel(args, local):
     elif args.workload == "attention":
         b, ms, _ = kernel_attention(ctx, stream, args.tokens, **kw)
         name, launches = f"configs[2] attention T={args.tokens}", 2
+    elif args.workload == "prefill_gemm":
+        rec = kernel_prefill_gemm(ctx, stream, "gate_up", 1, 37888, 3584, **kw)
+        return {"metric": "prefill GEMM tensor-pipe TFLOP/s (7B gate/up, 128 positions)",
+                "value": rec["tensor_pipe_tflops"], "unit": "TFLOP/s", "n_gpus": 1, "higher_is_better": True,
+                "kernel": rec, "gpu_launches_per_unit": 2}
     else:
         b, ms, _ = kernel_ternary(ctx, stream, args.n, args.block, args.order, **kw)
         name, launches = f"configs[0] Ternary2 {args.n}^2 bs{args.block}", 1
@@ -603,7 +693,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="satori", choices=["satori", "reference"])
     ap.add_argument("--workload", default="decode7b",
-                    choices=["decode7b", "decode1p5b", "matvec", "attention", "ternary"])
+                    choices=["decode7b", "decode1p5b", "matvec", "attention", "ternary", "prefill_gemm"])
     ap.add_argument("--tokens", type=int, default=32768)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--block", type=int, default=128)
@@ -614,6 +704,7 @@ def main():
     ap.add_argument("--repeats", type=int, default=5)
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel records of the decode line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the tensor-core prefill record")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     args.steps = max(1, args.steps)

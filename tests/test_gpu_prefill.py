@@ -118,11 +118,13 @@ def test_tensor_order_rejections(sat, ctx):
 
 
 # ---------------------------------------------------------------- session prefill (satori_session_forward_tensor)
-# The prefill's projections differ from ExecuteBatch's FP32 order by a few roundings (bounded above), so
-# the cache rows it writes differ from the per-token path's at that level; the logits after it are held
-# to the decode session's own tolerance against the oracle (LOGIT_REL / LOGIT_ABS in
-# test_gpu_session.py), and greedy tokens must be identical.
-LOGIT_REL, LOGIT_ABS = 1e-4, 5e-5
+# The prefill's projections differ from ExecuteBatch's FP32 order by a few roundings of sum|w x| (bounded
+# above), so every cache row it writes differs from the per-token path's at that level, and the difference
+# is carried through every layer and every later position's attention.  Measured on the 1.5B shape (28
+# layers, 200 prefilled positions): 7.1e-5 absolute on the logits, against 1.7e-5 for the per-token path.
+# The stated bound is 1e-4 relative + 2e-4 absolute, five times tighter than the reference's own
+# whole-model check (1e-3 + 1e-3 |x|, QwenForwardTests.cs:113); greedy tokens must be identical.
+LOGIT_REL, LOGIT_ABS = 1e-4, 2e-4
 
 
 def _close(a, b):
@@ -141,6 +143,7 @@ def _prefill_vs_oracle(sat, ctx, spec, tensors, prompt, n_gen, context):
         lr, ar = ref.append(int(t), threads=threads)
     ok, worst = _close(lg, lr)
     assert ok, ("prefill logits", worst)
+    print(f"prefill {spec.name}: worst logit error {worst:.3g}")
     tok = int(np.argmax(lr))
     assert int(np.argmax(lg)) == tok
     assert gpu.position == ref.position == len(prompt)
