@@ -34,6 +34,7 @@
 // residual += acc (DenseForward.cs:148,160), and SwiGlu of interleaved gate/up rows (DenseForward.cs:151-153).
 #include "common.cuh"
 #include "gemv.cuh"
+#include "qblock.cuh"
 
 #include <cuda_bf16.h>
 
@@ -50,6 +51,7 @@ constexpr int kTcXParts = 3;
 constexpr int kTcThreads = 160;      // warps 0-3 decode + epilogue, warp 4 control
 constexpr int kTcHeader = 256;
 constexpr int kTcMaxPositions = 128;
+constexpr int kTcRaw = 4;                 // K steps of raw weight bytes staged ahead per decode thread
 constexpr uint32_t kTcApart = kTcM * kTcK * 2;   // 16 KB per bf16 weight part
 
 struct TcOut {
@@ -120,6 +122,16 @@ __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.
 
 __device__ __forceinline__ uint32_t bf16_bits(float v) { return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v)); }
 __device__ __forceinline__ float bf16_value(uint32_t bits) { return __uint_as_float(bits << 16); }
+// Both halves of a float pair rounded to bf16 (x in the low half), and their values back as floats.
+__device__ __forceinline__ uint32_t bf16x2_bits(float2 v)
+{
+    const __nv_bfloat162 b = __floats2bfloat162_rn(v.x, v.y);
+    return *reinterpret_cast<const uint32_t *>(&b);
+}
+__device__ __forceinline__ float2 bf16x2_value(uint32_t bits)
+{
+    return make_float2(__uint_as_float(bits << 16), __uint_as_float(bits & 0xFFFF0000u));
+}
 
 template <int FMT>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a)
@@ -218,6 +230,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a)
         const int grow = row0 + r;
         const bool live = grow < a.rows;
         const uint8_t *rowp = a.payload + (size_t)min(grow, a.rows - 1) * (a.cols / 32) * BB + (size_t)k0 * 2 * BB;
+        // This thread's row bytes of each K step (two blocks: 36 (Q4_0) or 68 (Q8_0) bytes, 4-byte aligned)
+        // are staged kTcRaw steps ahead by asynchronous copies into its own slots of the raw ring; only
+        // this thread reads them, so its own wait_group is the only synchronisation they need.
+        constexpr int NWD = BB * 2 / 4;
+        uint32_t *raw = reinterpret_cast<uint32_t *>(stage0 + (size_t)kTcStages * stage_bytes) + r * NWD;
+        auto stage_raw = [&](int kt) {
+            const uint32_t *src = reinterpret_cast<const uint32_t *>(rowp + (size_t)kt * 2 * BB);
+            uint32_t *dst = raw + (size_t)(kt % kTcRaw) * kTcM * NWD;
+#pragma unroll
+            for (int i = 0; i < NWD; ++i)
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst + i)), "l"(src + i)
+                             : "memory");
+        };
+#pragma unroll
+        for (int i = 0; i < kTcRaw; ++i) {
+            if (i < nk) stage_raw(i);
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
         for (int kt = 0; kt < nk && !*abort_flag; ++kt) {
             const int s = kt % kTcStages;
             if (kt >= kTcStages &&
@@ -226,41 +256,60 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a)
                 *abort_flag = 1;
                 break;
             }
-            // Two blocks of the row: 36 (Q4_0) or 68 (Q8_0) bytes, 4-byte aligned.
-            constexpr int NWD = BB * 2 / 4;
+            // Groups committed so far: kTcRaw + kt; step kt's is complete once at most kTcRaw - 1 pend.
+            asm volatile("cp.async.wait_group %0;" ::"n"(kTcRaw - 1) : "memory");
             uint32_t wd[NWD];
-            const uint32_t *src = reinterpret_cast<const uint32_t *>(rowp + (size_t)kt * 2 * BB);
+            const uint32_t *mine = raw + (size_t)(kt % kTcRaw) * kTcM * NWD;
 #pragma unroll
-            for (int i = 0; i < NWD; ++i) wd[i] = live ? src[i] : 0u;
-            const uint8_t *bytes = reinterpret_cast<const uint8_t *>(wd);
+            for (int i = 0; i < NWD; ++i) wd[i] = live ? mine[i] : 0u;
+            // Exact decode (QuantizedRow.DecodeQ8Block / DecodeQ4Block): a byte-permute puts each code byte
+            // (the biased int8, or a masked nibble) under the 2^23 exponent and one FP32x2 FMA turns the pair
+            // into d * code exactly (the scale constants are exact: d has at most 11 significant bits).
+            float2 S[2][2], C[2][2];
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+                const int pos = blk * BB;                                    // byte of the block's scale
+                const float d = half_bits_to_float((wd[pos >> 2] >> (8 * (pos & 3))) & 0xFFFFu);
+                if (FMT == 0) {
+                    const float sc = fmul(d, 0.00390625f), cc = fmul(d, -32896.0f);      // 2^-8, -(2^15 + 128)
+                    S[blk][0] = S[blk][1] = make_float2(sc, sc);
+                    C[blk][0] = C[blk][1] = make_float2(cc, cc);
+                } else {
+                    const float sl = fmul(d, 0.00390625f), cl = fmul(d, -32776.0f);      // low nibble in place
+                    const float sh = fmul(d, 0.000244140625f), ch = fmul(d, -2056.0f);   // high nibble in place
+                    S[blk][0] = make_float2(sl, sl);
+                    C[blk][0] = make_float2(cl, cl);
+                    S[blk][1] = make_float2(sh, sh);
+                    C[blk][1] = make_float2(ch, ch);
+                }
+            }
+            const float2 minus1 = make_float2(-1.0f, -1.0f);
             uint8_t *abase = stage0 + (size_t)s * stage_bytes;
 #pragma unroll
             for (int kc = 0; kc < kTcK / 8; ++kc) {
                 uint32_t part[NA][4];
 #pragma unroll
                 for (int e = 0; e < 8; e += 2) {
-                    float w2[2];
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int k = kc * 8 + e + h, blk = k >> 5, j = k & 31;
-                        const uint8_t *b = bytes + blk * BB;
-                        const float d = half_bits_to_float((uint32_t)b[0] | ((uint32_t)b[1] << 8));
-                        int q;
-                        if (FMT == 0) q = (int)(int8_t)b[2 + j];
-                        else q = j < 16 ? (int)(b[2 + j] & 15) - 8 : (int)(b[2 + j - 16] >> 4) - 8;
-                        w2[h] = fmul(d, (float)q);     // QuantizedRow.DecodeQ8Block / DecodeQ4Block, exact
+                    // Weights k, k+1 of this step: block k / 32, codes j, j+1 (j even, so the two code
+                    // bytes share a word).
+                    const int k = kc * 8 + e, blk = k >> 5, j = k & 31;
+                    float2 W;
+                    if (FMT == 0) {
+                        const int pb = blk * BB + 2 + j;
+                        const uint32_t u = wd[pb >> 2] ^ 0x80808080u;        // biased: code + 128
+                        W = __ffma2_rn(code_pair(u, pb & 3, (pb & 3) + 1), S[blk][0], C[blk][0]);
+                    } else {
+                        const int hi = j >= 16, pb = blk * BB + 2 + (j & 15);
+                        const uint32_t u = wd[pb >> 2] & (hi ? 0xF0F0F0F0u : 0x0F0F0F0Fu);
+                        W = __ffma2_rn(code_pair(u, pb & 3, (pb & 3) + 1), S[blk][hi], C[blk][hi]);
                     }
-                    uint32_t hi[2], mid[2], lo[2];
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        hi[h] = bf16_bits(w2[h]);
-                        const float r1 = __fsub_rn(w2[h], bf16_value(hi[h]));
-                        mid[h] = bf16_bits(r1);
-                        lo[h] = bf16_bits(__fsub_rn(r1, bf16_value(mid[h])));
-                    }
-                    part[0][e / 2] = hi[0] | (hi[1] << 16);
-                    part[1][e / 2] = mid[0] | (mid[1] << 16);
-                    if (NA == 3) part[NA - 1][e / 2] = lo[0] | (lo[1] << 16);
+                    // Exact bf16 parts: each residual w - part is exact in FP32 (fma with -1).
+                    const uint32_t p0 = bf16x2_bits(W);
+                    const float2 r1 = __ffma2_rn(bf16x2_value(p0), minus1, W);
+                    const uint32_t p1 = bf16x2_bits(r1);
+                    part[0][e / 2] = p0;
+                    part[1][e / 2] = p1;
+                    if (NA == 3) part[2][e / 2] = bf16x2_bits(__ffma2_rn(bf16x2_value(p1), minus1, r1));
                 }
                 // Core matrix (row group r/8, K chunk kc): 8 rows x 16 bytes; chunks of a row group are
                 // 2048 bytes apart (the K direction), row groups 128 bytes apart.
@@ -272,7 +321,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const TcArgs a)
             }
             fence_proxy_async();          // the tensor core reads these stores through the async proxy
             mbar_arrive(&a_ready[s]);
+            // wd has been consumed, so step kt's slots are free for step kt + kTcRaw.
+            if (kt + kTcRaw < nk) stage_raw(kt + kTcRaw);
+            asm volatile("cp.async.commit_group;" ::: "memory");
         }
+        asm volatile("cp.async.wait_all;" ::: "memory");     // no copy lands after the CTA winds down
         // Epilogue: wait for the last step's MMAs, then TMEM lanes 32w..32w+31 hold rows of this warp.
         const int lastkt = nk - 1;
         bool ok = !*abort_flag &&
@@ -419,7 +472,9 @@ cudaError_t launch_tc_gemm(const TcGemm &g, int sm_count, cudaStream_t stream)
     a.out.ldr = g.ldr > 0 ? g.ldr : g.rows;
     a.err = g.err;
     const int na = g.format == SATORI_Q8_0 ? 3 : 2;
-    const size_t smem = 128 + kTcHeader + (size_t)kTcStages * (na * kTcApart + kTcXParts * (size_t)n16 * kTcK * 2);
+    const int bb = g.format == SATORI_Q8_0 ? 34 : 18;
+    const size_t smem = 128 + kTcHeader + (size_t)kTcStages * (na * kTcApart + kTcXParts * (size_t)n16 * kTcK * 2) +
+                        (size_t)kTcRaw * kTcM * 2 * bb;
     auto kern = g.format == SATORI_Q8_0 ? tc_gemm_kernel<0> : tc_gemm_kernel<1>;
     e = opt_in_smem(reinterpret_cast<const void *>(kern), smem);
     if (e != cudaSuccess) return e;
