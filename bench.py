@@ -620,6 +620,24 @@ def bench_decode(args, rank, world, local, spec, with_kernels: bool):
     return res
 
 
+def bench_prefill(args, local):
+    """The 7B tensor-core prefill alone (profiling): a --prompt-token satori_session_forward_tensor."""
+    import torch
+
+    import satori_b200 as sat
+    ctx = sat.Context(local)
+    spec = sat.qwen2_7b()
+    tensors = device_model(ctx, spec, seed=31)
+    torch.cuda.synchronize()
+    sess = sat.CudaDenseSession(spec, tensors, args.prompt + 8, ctx=ctx)
+    del tensors
+    torch.cuda.empty_cache()
+    rec = prefill_record(sess, spec, args.prompt, ctx, repeats=args.repeats)
+    sess.dispose()
+    return {"metric": f"prefill tokens/s ({spec.name}, {args.prompt}-token prompt, tensor cores)",
+            "value": rec["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True, "prefill": rec}
+
+
 # ------------------------------------------------------------------ single-kernel workloads (profiling)
 def bench_kernel(args, local):
     import torch
@@ -693,7 +711,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="satori", choices=["satori", "reference"])
     ap.add_argument("--workload", default="decode7b",
-                    choices=["decode7b", "decode1p5b", "matvec", "attention", "ternary", "prefill_gemm"])
+                    choices=["decode7b", "decode1p5b", "prefill7b", "matvec", "attention", "ternary", "prefill_gemm"])
     ap.add_argument("--tokens", type=int, default=32768)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--block", type=int, default=128)
@@ -721,6 +739,8 @@ def main():
     if args.workload in ("decode7b", "decode1p5b"):
         spec = sat.qwen2_7b() if args.workload == "decode7b" else sat.qwen2_1_5b()
         res = bench_decode(args, rank, world, local, spec, with_kernels=not args.no_kernels)
+    elif args.workload == "prefill7b":
+        res = bench_prefill(args, local) if rank == 0 else None
     else:
         res = bench_kernel(args, local) if rank == 0 else None
     if rank == 0 and res is not None:

@@ -531,6 +531,196 @@ __global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
     }
 }
 
+// Prefill: the positions of a chunk attend to nearly the same prefix, so one CTA serves 8 consecutive
+// positions of one KV head (warp w = position zb + w) and every K/V tile it streams is read by all 8
+// warps from shared memory.  The CTA's token range [t0, t1) is split s of the LONGEST prefix of its
+// positions; position z uses [t0, min(t1, T_z)) and writes its own split record (an empty range gives
+// m = -inf, l = 0, which the merge weighs as zero).  Per token and head the arithmetic is the stream
+// kernel's (FP32x2 dot, transposed butterfly, online softmax, FP32x2 p.v).
+constexpr int kPrefillPos = kStreamWarps;            // positions per CTA
+
+__global__ void __launch_bounds__((kStreamWarps + 1) * 32, 1)
+    attn_prefill_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                        const AttnParams p)
+{
+    constexpr int GMAX = 8, DPL = 4, R = 32 / GMAX;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + kStreamSlots;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStreamSlots);
+    float (*P)[kStreamTok][GMAX] = reinterpret_cast<float (*)[kStreamTok][GMAX]>(smem + kStreamHeader);
+    uint8_t *slots = smem + kStreamHeader + kStreamPBytes;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int split = blockIdx.x;
+    const int kvh = blockIdx.y / p.ngroups, grp = blockIdx.y % p.ngroups;
+    const int h0 = kvh * p.group + grp * GMAX;
+    const int gc = min(GMAX, p.group - grp * GMAX);
+    const int hd = 128;
+    const int hl = lane / R;
+    const int zb = blockIdx.z * kPrefillPos;
+    const int nz = min(kPrefillPos, p.batch - zb);             // positions of this CTA
+
+    if (tid == 0) {
+        *abort_flag = 0;
+        for (int s = 0; s < kStreamSlots; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kStreamWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (p.use_pdl) {
+        pdl_launch_dependents();
+        pdl_wait();
+    }
+    const int Tmax = p.tokens + zb + nz - 1;                   // prefix of the CTA's last position
+    const int t0 = (int)(((long long)Tmax * split) / p.nsplit);
+    const int t1 = (int)(((long long)Tmax * (split + 1)) / p.nsplit);
+    const int nst = (t1 - t0 + kStreamTok - 1) / kStreamTok;
+
+    if (warp == kStreamWarps) {
+        if (lane == 0) {
+            auto issue = [&](int k) {
+                const int s = k % kStreamSlots;
+                uint8_t *dst = slots + (size_t)s * 2 * kStreamTileBytes;
+                mbar_expect_tx(&full[s], 2u * kStreamTileBytes);
+                tma_load_3d(dst, &kmap, 0, kvh, t0 + k * kStreamTok, &full[s]);
+                tma_load_3d(dst + kStreamTileBytes, &vmap, 0, kvh, t0 + k * kStreamTok, &full[s]);
+            };
+            prefetch_tensormap(&kmap);
+            prefetch_tensormap(&vmap);
+            const int first = min(kStreamSlots, nst);
+            for (int k = 0; k < first; ++k) issue(k);
+            int k = 0;
+            for (; k + kStreamSlots < nst; ++k) {
+                if (*abort_flag || !mbar_wait_bounded(&empty[k % kStreamSlots], (uint32_t)((k / kStreamSlots) & 1))) {
+                    if (p.err) atomicOr(p.err, kDevErrTimeout);
+                    *abort_flag = 1;
+                    break;
+                }
+                issue(k + kStreamSlots);
+            }
+            const int last = min(k + kStreamSlots, nst) - 1;
+            for (int j = max(0, last - kStreamSlots + 1); j <= last; ++j)
+                mbar_wait_bounded(&full[j % kStreamSlots], (uint32_t)((j / kStreamSlots) & 1));
+        }
+        return;
+    }
+
+    // Compute warp: position z = zb + warp (idle but still pacing the ring when z is past the batch).
+    const int z = zb + warp;
+    const bool live = warp < nz;
+    const int Tz = p.tokens + z;
+    const int tend = live ? min(t1, Tz) : t0;                  // this position's tokens: [t0, tend)
+    const float *q = p.q + (long long)(live ? z : zb) * p.q_pstride;
+    float2 qp[GMAX / 2][DPL];
+#pragma unroll
+    for (int g = 0; g < GMAX / 2; ++g)
+#pragma unroll
+        for (int i = 0; i < DPL; ++i)
+            qp[g][i] = make_float2(2 * g < gc ? q[(h0 + 2 * g) * hd + 4 * lane + i] : 0.0f,
+                                   2 * g + 1 < gc ? q[(h0 + 2 * g + 1) * hd + 4 * lane + i] : 0.0f);
+    float2 acc[GMAX][DPL / 2];
+#pragma unroll
+    for (int h = 0; h < GMAX; ++h)
+#pragma unroll
+        for (int c = 0; c < DPL / 2; ++c) acc[h][c] = make_float2(0.0f, 0.0f);
+    float m_my = -INFINITY, l_my = 0.0f;
+    for (int k = 0; k < nst; ++k) {
+        const int s = k % kStreamSlots;
+        if (*abort_flag) break;
+        if (!mbar_wait_bounded(&full[s], (uint32_t)((k / kStreamSlots) & 1))) {
+            if (p.err) atomicOr(p.err, kDevErrTimeout);
+            *abort_flag = 1;
+            break;
+        }
+        const int tb = t0 + k * kStreamTok;
+        const int nt = min(kStreamTok, tend - tb);                 // <= 0: past this position's prefix
+        if (nt > 0) {
+            const uint32_t kt = smem_u32(slots + (size_t)s * 2 * kStreamTileBytes) + 16u * lane;
+            const uint32_t vt = kt + kStreamTileBytes;
+            float sc[kStreamTok];
+#pragma unroll
+            for (int j = 0; j < kStreamTok; ++j) {
+                if (j < nt) {
+                    const float4 t4 = lds128f(kt + 512u * j);
+                    const float kr[DPL] = {t4.x, t4.y, t4.z, t4.w};
+                    float v[8];
+#pragma unroll
+                    for (int g = 0; g < GMAX / 2; ++g) {
+                        float2 a = make_float2(0.0f, 0.0f);
+#pragma unroll
+                        for (int i = 0; i < DPL; ++i) a = __ffma2_rn(qp[g][i], make_float2(kr[i], kr[i]), a);
+                        v[2 * g] = a.x;
+                        v[2 * g + 1] = a.y;
+                    }
+                    sc[j] = transpose_reduce<GMAX>(v, lane) * p.scale;
+                } else {
+                    sc[j] = -INFINITY;
+                }
+            }
+            float mb = sc[0];
+#pragma unroll
+            for (int j = 1; j < kStreamTok; ++j) mb = fmaxf(mb, sc[j]);
+            const float m_new = fmaxf(m_my, mb);
+            const float alpha = m_my == -INFINITY ? 0.0f : expf(m_my - m_new);
+            float lsum = 0.0f;
+#pragma unroll
+            for (int j = 0; j < kStreamTok; ++j) {
+                const float pj = j < nt ? expf(sc[j] - m_new) : 0.0f;
+                lsum += pj;
+                if ((j % R) == (lane % R)) P[warp][j][hl] = pj;
+            }
+            l_my = l_my * alpha + lsum;
+            m_my = m_new;
+#pragma unroll
+            for (int h = 0; h < GMAX; ++h) {
+                const float ah = __shfl_sync(0xFFFFFFFFu, alpha, h * R);
+#pragma unroll
+                for (int c = 0; c < DPL / 2; ++c) acc[h][c] = __fmul2_rn(acc[h][c], make_float2(ah, ah));
+            }
+            __syncwarp();
+            for (int j = 0; j < nt; ++j) {
+                const float4 t4 = lds128f(vt + 512u * j);
+                const float2 v01 = make_float2(t4.x, t4.y), v23 = make_float2(t4.z, t4.w);
+                const float4 pa = *reinterpret_cast<const float4 *>(&P[warp][j][0]);
+                const float4 pb = *reinterpret_cast<const float4 *>(&P[warp][j][4]);
+                const float pj[GMAX] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+                for (int h = 0; h < GMAX; ++h) {
+                    const float2 pp = make_float2(pj[h], pj[h]);
+                    acc[h][0] = __ffma2_rn(pp, v01, acc[h][0]);
+                    acc[h][1] = __ffma2_rn(pp, v23, acc[h][1]);
+                }
+            }
+            __syncwarp();
+        }
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (!live) return;
+    // This position's record of this split; an expired wait leaves NaN for the merge's FP64 recompute.
+    const bool aborted = *abort_flag != 0;
+    const int rs = hd + 2;
+    float *rec = p.scratch + (long long)z * p.nsplit * p.q_heads * rs + (long long)split * p.q_heads * rs;
+    const float nan = __int_as_float(0x7fc00000);
+    if (lane % R == 0 && hl < gc) {
+        rec[(h0 + hl) * rs] = aborted ? nan : m_my;
+        rec[(h0 + hl) * rs + 1] = aborted ? nan : l_my;
+    }
+#pragma unroll
+    for (int h = 0; h < GMAX; ++h) {
+        if (h < gc) {
+            float *w = rec + (h0 + h) * rs + 2 + 4 * lane;
+            w[0] = aborted ? nan : acc[h][0].x;
+            w[1] = aborted ? nan : acc[h][0].y;
+            w[2] = aborted ? nan : acc[h][1].x;
+            w[3] = aborted ? nan : acc[h][1].y;
+        }
+    }
+}
+
 // Split records are merged in chunks staged through shared memory with cp.async, so every record
 // load of a chunk is in flight at once (a thread walking the splits one global load at a time is
 // latency-bound).  The arithmetic and its order are unchanged: max over splits, then l and each output
@@ -727,10 +917,21 @@ int attn_splits(int q_heads, int kv_heads, int head_dim, int max_tokens, int sm_
     return nsplit;
 }
 
+// Splits of the prefill kernel: about two CTAs per SM over (KV head group, 8-position block, split),
+// at least 64 tokens per split of the longest prefix.
+int attn_prefill_splits(int q_heads, int kv_heads, int max_tokens, int sm_count, int batch)
+{
+    const int group = q_heads / kv_heads;
+    const int units = kv_heads * ((group + 7) / 8) * ((batch + kPrefillPos - 1) / kPrefillPos);
+    int nsplit = std::max(1, (2 * sm_count + units - 1) / units);
+    return std::min(nsplit, std::max(1, max_tokens / 64));
+}
+
 size_t attn_scratch_floats(int q_heads, int kv_heads, int head_dim, int max_tokens, int sm_count, int batch)
 {
-    return (size_t)attn_splits(q_heads, kv_heads, head_dim, max_tokens, sm_count, batch) * q_heads *
-           (head_dim + 2) * std::max(1, batch);
+    int splits = attn_splits(q_heads, kv_heads, head_dim, max_tokens, sm_count, batch);
+    if (batch > 1) splits = std::max(splits, attn_prefill_splits(q_heads, kv_heads, max_tokens, sm_count, batch));
+    return (size_t)splits * q_heads * (head_dim + 2) * std::max(1, batch);
 }
 
 namespace {
@@ -777,6 +978,19 @@ bool launch_stream(const AttnArgs &a, AttnParams &p, int gmax, int sm_count, cud
     if (!encode_kv_map(&kmap, a.keys, a.kv_heads, p.kv_stride, cap) ||
         !encode_kv_map(&vmap, a.values, a.kv_heads, p.kv_stride, cap))
         return false;
+    if (p.batch > 1) {
+        // A prefill chunk: 8 positions per CTA share every K/V tile.
+        p.nsplit = attn_prefill_splits(a.q_heads, a.kv_heads, a.tokens + p.batch - 1, sm_count, p.batch);
+        const cudaError_t e = opt_in_smem(reinterpret_cast<const void *>(attn_prefill_kernel), kStreamSmem);
+        if (e != cudaSuccess) {
+            *err = e;
+            return true;
+        }
+        attn_prefill_kernel<<<dim3(p.nsplit, units, (p.batch + kPrefillPos - 1) / kPrefillPos),
+                              (kStreamWarps + 1) * 32, kStreamSmem, stream>>>(kmap, vmap, p);
+        *err = cudaGetLastError();
+        return true;
+    }
     // About one CTA per SM (each keeps ~64 KB in flight); never more splits than the scratch holds.
     p.nsplit = std::max(1, std::min(p.nsplit, (sm_count + units * p.batch - 1) / (units * p.batch)));
     const cudaError_t e = opt_in_smem(reinterpret_cast<const void *>(attn_stream_kernel), kStreamSmem);
