@@ -102,3 +102,29 @@ def test_noalloc_rejects_shapes_beyond_its_fixed_scratch(env):
                                                 out.data_ptr(), None)
     assert status == _lib.ERR_ARGUMENT
     assert "scratch" in _lib.last_error()
+
+
+def test_noalloc_on_two_devices_in_one_process(env):
+    """The shared-memory opt-in of the attention kernels is held per device: a call on device 1 after one
+    on device 0 (one process, one library) still launches, and gives the same bits as device 0."""
+    sat, _lib, torch = env
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    L = _lib.lib()
+    qh, kvh, hd, T = 28, 4, 128, 1500
+    outs = []
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            g = torch.Generator(device="cuda").manual_seed(5)
+            q = torch.randn(qh * hd, generator=g, device="cuda")
+            k = torch.randn(T * kvh * hd, generator=g, device="cuda")
+            v = torch.randn(T * kvh * hd, generator=g, device="cuda")
+            out = torch.full((qh * hd,), float("nan"), device="cuda")
+            torch.cuda.synchronize()
+            _lib.check(L.satori_grouped_attention_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), qh, kvh, hd, T,
+                                                          out.data_ptr(), torch.cuda.current_stream().cuda_stream),
+                       f"noalloc on device {dev}")
+            torch.cuda.synchronize()
+            outs.append(out.cpu().numpy())
+    assert np.all(np.isfinite(outs[1]))
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
