@@ -57,7 +57,8 @@ def test_quantized_shape_rules():
             QuantizedMatrixShape(bad[0], bad[1], 0)
 
 
-def test_ternary2_geometry_matches_survey_figures():
+def test_ternary2_geometry_matches_benchmark_byte_counts():
+    """Ternary2Shape.ByteLength (Ternary2Shape.cs:14) at the benchmark shapes."""
     from satori_b200 import ternary2_byte_length
     assert ternary2_byte_length(4096, 4096, 64) == 5242880
     assert ternary2_byte_length(4096, 4096, 128) == 4718592
