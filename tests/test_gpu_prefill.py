@@ -246,3 +246,28 @@ def test_qwen2_7b_shape_prefill_matches_per_token_path(sat, ctx, oracle_lib):
     assert list(a.generate(first, 8)) == list(b.generate(first, 8))
     a.dispose()
     b.dispose()
+
+
+def test_prefill_with_per_head_norms_matches_per_token_path(sat, ctx, oracle_lib):
+    """qwen3-style layers (no q/k/v bias, attn_q_norm / attn_k_norm per head, DenseForward.cs:130-133): the
+    chunk's batched head norms against the decode step's (TransformerOps.RmsNormHeads, pinned by the
+    reference's qk_norm fixture); logits within the prefill tolerance and greedy tokens identical."""
+    from model_util import synthetic_tensors
+    spec = sat.tiny(layers=2, q_heads=8, kv_heads=2, head_dim=128, hidden=512, ffn=1024, has_bias=False)
+    tensors = synthetic_tensors(spec, 61)
+    rng = np.random.default_rng(62)
+    for l in range(spec.layers):
+        for part in ("q", "k"):
+            tensors[f"blk.{l}.attn_{part}_norm.weight"] = (1.0 + 0.1 * rng.standard_normal(spec.head_dim)).astype(
+                np.float32)
+    prompt = rng.integers(0, spec.vocab, 150)
+    a = sat.CudaDenseSession(spec, tensors, 200, ctx=ctx)
+    b = sat.CudaDenseSession(spec, tensors, 200, ctx=ctx)
+    la = a.forward(prompt, tensor_cores=True)
+    lb = b.forward(prompt)
+    ok, worst = _close(la, lb)
+    assert ok and int(np.argmax(la)) == int(np.argmax(lb)), worst
+    first = int(np.argmax(lb))
+    assert list(a.generate(first, 10)) == list(b.generate(first, 10))
+    a.dispose()
+    b.dispose()
