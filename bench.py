@@ -247,6 +247,44 @@ def kernel_matvec(ctx, stream, copies=12, **kw):
     return step_bytes, ms
 
 
+DECODE_SHAPES = [("lm_head", 0, 152064, 3584), ("gate_up", 1, 37888, 3584), ("down", 1, 3584, 18944),
+                 ("qkv", 1, 4608, 3584)]
+
+
+def kernel_matvec_shape(ctx, stream, fmt, rows, cols, **kw):
+    """One 7B decode projection alone (decode order, one position), rotating enough weight copies that
+    the working set exceeds L2 four times over."""
+    import torch
+
+    import satori_b200 as sat
+    from satori_b200 import _lib
+    nbytes = rows * (cols // 32) * (34 if fmt == 0 else 18)
+    copies = max(1, int(math.ceil(4 * 126e6 / nbytes)))
+    base = device_quantized(ctx, rows, cols, fmt, seed=rows + fmt)
+    mats = [sat.CudaQuantizedMatrix.from_device(ctx, base.data_ptr(), base.numel(), rows, cols, fmt)]
+    for c in range(1, copies):
+        mats.append(sat.CudaQuantizedMatrix.from_device(ctx, base.data_ptr(), base.numel(), rows, cols, fmt))
+    del base
+    x = torch.randn(cols, generator=torch.Generator(device="cuda").manual_seed(9), device="cuda")
+    y = torch.empty(rows, device="cuda")
+    torch.cuda.synchronize()
+    ctx.set_stream(stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        mats[0].execute_device(x.data_ptr(), y.data_ptr(), 1, _lib.ORDER_BATCH)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for m in mats:
+            m.execute_device(x.data_ptr(), y.data_ptr(), 1, _lib.ORDER_BATCH)
+    torch.cuda.synchronize()
+    ms = repeat_regions(graph.replay, stream, copies, **kw)
+    ctx.set_stream(None)
+    del graph
+    for m in mats:
+        m.dispose()
+    return nbytes, ms, copies
+
+
 def kernel_attention(ctx, stream, T, **kw):
     """GQA 28/4 x 128 over T cached tokens (stream + merge launches), rotating layers."""
     import torch
@@ -410,6 +448,11 @@ def kernels_record(ctx, min_region_s=0.5, repeats=5):
     out["matvec_q8_0_4096x4096+q4_0_11008x4096"] = stats_record(
         b, ms, peak, kind, {"workload": "configs[1]", "launches_per_unit": 2,
                             "order": "ExecuteBatch (decode), bit-exact"})
+    for name, fmt, rows, cols in DECODE_SHAPES:
+        b, ms, copies = kernel_matvec_shape(ctx, stream, fmt, rows, cols, **kw)
+        out[f"matvec_7b_{name}_{'q8_0' if fmt == 0 else 'q4_0'}_{rows}x{cols}"] = stats_record(
+            b, ms, peak, kind, {"workload": "configs[4] decode projection", "copies": copies,
+                                "order": "ExecuteBatch (decode), bit-exact"})
     for T in (512, 4096, 32768):
         b, ms, layers = kernel_attention(ctx, stream, T, **kw)
         out[f"attention_T{T}"] = stats_record(b, ms, peak, kind, {"workload": f"configs[2] 28/4 x 128, T={T}",
