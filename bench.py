@@ -663,6 +663,57 @@ def bench_decode(args, rank, world, local, spec, with_kernels: bool):
     return res
 
 
+def bench_matvec_sharded(args, rank, world, local):
+    """The row-sharded large MatVec (Q4_0 11008x4096, decode order) over N GPUs: every rank computes its
+    contiguous row block and NCCL all-gathers y (satori_matrix_sharded_execute_device).  Each timed call
+    follows an untimed write of a 256 MB buffer (L2 flushed: a rank's slice alone would fit in L2);
+    device time of the calls only, max over ranks; value = the whole matrix's payload bytes per call time."""
+    import torch
+
+    import satori_b200 as sat
+    from satori_b200 import _lib
+    ctx = sat.Context(local)
+    rows, cols, fmt = 11008, 4096, 1
+    dev = device_quantized(ctx, rows, cols, fmt, seed=123)          # the same bytes on every rank
+    nccl_id = sat.broadcast_nccl_id() if world > 1 else None
+    m = sat.CudaShardedMatrix(ctx, dev, sat.QuantizedMatrixShape(rows, cols, fmt), rank, world, nccl_id)
+    del dev
+    x = torch.randn(cols, generator=torch.Generator(device="cuda").manual_seed(7), device="cuda")
+    y = torch.empty(rows, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    ext = torch.cuda.ExternalStream(ctx.stream)
+    for _ in range(args.warmup):
+        m.execute_device(x.data_ptr(), y.data_ptr(), _lib.ORDER_BATCH)
+    torch.cuda.synchronize()
+    dist_barrier(world)
+    total = 0.0
+    with ClockSampler(local) as clocks:
+        for _ in range(args.steps):
+            with torch.cuda.stream(ext):
+                flush.fill_(1)
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(ext)
+            m.execute_device(x.data_ptr(), y.data_ptr(), _lib.ORDER_BATCH)
+            end.record(ext)
+            torch.cuda.synchronize()
+            total += start.elapsed_time(end)
+    ms = dist_max(total / args.steps, world)
+    nbytes = rows * (cols // 32) * 18
+    m.dispose()
+    peak, kind = _peaks()
+    gbs = nbytes / (ms / 1e3) / GB
+    return {"metric": "row-sharded MatVec payload GB/s (Q4_0 11008x4096 + all-gather of y)",
+            "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "q4_0 weights, f32 activations", "data": "synthetic: seeded N(0,0.02^2) weights",
+            "config": {"workload": "configs[1] Q4_0 11008x4096, rows sharded over the GPUs",
+                       "l2_policy": "256 MB buffer written before every timed call",
+                       "parallelism": f"row shards x{world} + NCCL all-gather"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_kind": kind, "traffic": None},
+            "gpu_launches": 2 * args.steps, "clocks": clocks.summary()}
+
+
 def bench_prefill(args, local):
     """The 7B tensor-core prefill alone (profiling): a --prompt-token satori_session_forward_tensor."""
     import torch
@@ -754,7 +805,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="satori", choices=["satori", "reference"])
     ap.add_argument("--workload", default="decode7b",
-                    choices=["decode7b", "decode1p5b", "prefill7b", "matvec", "attention", "ternary", "prefill_gemm"])
+                    choices=["decode7b", "decode1p5b", "prefill7b", "matvec_sharded", "matvec", "attention", "ternary",
+                             "prefill_gemm"])
     ap.add_argument("--tokens", type=int, default=32768)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--block", type=int, default=128)
@@ -784,6 +836,8 @@ def main():
         res = bench_decode(args, rank, world, local, spec, with_kernels=not args.no_kernels)
     elif args.workload == "prefill7b":
         res = bench_prefill(args, local) if rank == 0 else None
+    elif args.workload == "matvec_sharded":
+        res = bench_matvec_sharded(args, rank, world, local)
     else:
         res = bench_kernel(args, local) if rank == 0 else None
     if rank == 0 and res is not None:

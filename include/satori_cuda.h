@@ -212,6 +212,25 @@ SATORI_API int satori_session_create_sharded(satori_ctx *ctx, const satori_model
                                              int world, const void *nccl_unique_id, satori_session **out);
 /* ncclGetUniqueId through the NCCL library loaded at run time (128 bytes into out128). */
 SATORI_API int satori_nccl_unique_id(void *out128);
+
+/* One large MatVec split by rows over the GPUs of a node (the row-sharded GEMV with an all-gather of y):
+ * IQuantizedMatrix.Execute (IQuantizedMatrix.cs:6) / QuantizedMatVec.ExecuteBatch (QuantizedMatVec.cs:104-120)
+ * with rank r of `world` holding rows [r*S, min((r+1)*S, rows)), S = ceil(rows / world).  `payload` is the
+ * WHOLE matrix (host, or device when payload_on_device), of which only this rank's rows are uploaded;
+ * every rank passes the same NCCL id (satori_nccl_unique_id on rank 0).  Execute computes this rank's rows
+ * with the single-GPU kernels (each row bit-exact to the reference in `order`) and all-gathers the full
+ * y[rows] onto every rank over NCCL; all ranks call it together.  Every rank must receive at least one
+ * row (SATORI_ERR_NOT_SUPPORTED otherwise). */
+typedef struct satori_matrix_sharded satori_matrix_sharded;
+SATORI_API int satori_matrix_create_sharded(satori_ctx *ctx, const uint8_t *payload, size_t bytes, int rows, int cols,
+                                            int format, int payload_on_device, int rank, int world,
+                                            const void *nccl_unique_id, satori_matrix_sharded **out);
+/* dx [cols], dy [rows] on this rank's device; the context's stream. */
+SATORI_API int satori_matrix_sharded_execute_device(satori_matrix_sharded *m, const float *dx, float *dy, int order);
+/* Host vectors, synchronous; y committed only on success. */
+SATORI_API int satori_matrix_sharded_execute(satori_matrix_sharded *m, const float *x, float *y, int order);
+SATORI_API int satori_matrix_sharded_info(const satori_matrix_sharded *m, int *row_begin, int *row_end);
+SATORI_API int satori_matrix_sharded_destroy(satori_matrix_sharded *m);
 /* DenseSession.Append (DenseSession.cs:111-131) + GreedyTokenSelector.Select
  * (src/Satori.Core/GreedyTokenSelector.cs:6-16): logits (host, may be NULL) and argmax (may be NULL). */
 SATORI_API int satori_session_append(satori_session *s, int token, float *logits, int *argmax);

@@ -6,7 +6,7 @@ The compute lives in ``_build/libsatori_cuda.so`` (hand-written sm_100a CUDA beh
 from ._lib import (ArgumentError, ContextFullError, DeviceError, DisposedError, InvalidDataError,
                    NotSupportedError, SatoriError, ORDER_BATCH, ORDER_EXECUTE, ORDER_SCALAR, Q4_0, Q8_0, Q4_K, Q6_K,
                    T2_64, T2_128, T2_256, version)
-from .core import (AttentionCache, BlockQuantization, Context, CudaMatrixFactory, CudaQuantizedMatrix,
+from .core import (AttentionCache, BlockQuantization, Context, CudaMatrixFactory, CudaQuantizedMatrix, CudaShardedMatrix,
                    MappedTernary2Matrix, QuantizedMatrixShape, Ternary2Matrix, Ternary2MatVec, TernaryBitplaneMatrix,
                    TernaryBitplaneMatVec, TransformerOps,
                    default_context, stq2_header, stq2_read_header, ternary2_byte_length)
@@ -18,6 +18,7 @@ __all__ = [
     "ArgumentError", "ContextFullError", "DeviceError", "DisposedError", "InvalidDataError", "NotSupportedError",
     "SatoriError", "ORDER_BATCH", "ORDER_EXECUTE", "ORDER_SCALAR", "Q4_0", "Q8_0", "Q4_K", "Q6_K", "T2_64", "T2_128", "T2_256",
     "version", "AttentionCache", "BlockQuantization", "Context", "CudaMatrixFactory", "CudaQuantizedMatrix",
+    "CudaShardedMatrix",
     "MappedTernary2Matrix", "QuantizedMatrixShape", "Ternary2Matrix", "Ternary2MatVec", "TernaryBitplaneMatrix",
     "TernaryBitplaneMatVec", "TransformerOps",
     "default_context", "stq2_header", "stq2_read_header", "ternary2_byte_length", "CudaDenseSession", "ModelSpec",

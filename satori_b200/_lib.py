@@ -117,6 +117,12 @@ _SIGS = {
     "satori_session_create_sharded": (C.c_int, [_vp, C.POINTER(ModelDesc), C.c_int, C.c_int, C.c_int, _vp,
                                                 C.POINTER(_vp)]),
     "satori_nccl_unique_id": (C.c_int, [_vp]),
+    "satori_matrix_create_sharded": (C.c_int, [_vp, _vp, C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                              _vp, C.POINTER(_vp)]),
+    "satori_matrix_sharded_execute_device": (C.c_int, [_vp, _vp, _vp, C.c_int]),
+    "satori_matrix_sharded_execute": (C.c_int, [_vp, _vp, _vp, C.c_int]),
+    "satori_matrix_sharded_info": (C.c_int, [_vp, _i32p, _i32p]),
+    "satori_matrix_sharded_destroy": (C.c_int, [_vp]),
     "satori_session_append": (C.c_int, [_vp, C.c_int, _vp, _i32p]),
     "satori_session_append_tokens": (C.c_int, [_vp, _vp, C.c_int, _vp, _i32p]),
 "satori_session_forward_tensor": (C.c_int, [_vp, _vp, C.c_int, _vp, _i32p]),

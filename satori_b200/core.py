@@ -257,6 +257,58 @@ class CudaQuantizedMatrix:
             pass
 
 
+class CudaShardedMatrix:
+    """One large MatVec split by rows over the GPUs of a node (one process per GPU): rank r holds rows
+    [r*S, min((r+1)*S, rows)), S = ceil(rows / world), computes them with the single-GPU kernels (each row
+    bit-exact in the requested order) and NCCL all-gathers the full output onto every rank.  Every rank
+    passes the WHOLE payload (only its rows are uploaded) and the same NCCL id; execute is a collective."""
+
+    def __init__(self, ctx: Context, payload, shape: QuantizedMatrixShape, rank: int, world: int, nccl_id: bytes):
+        self.ctx = ctx
+        self.rows, self.columns, self.format = shape.rows, shape.columns, int(shape.format)
+        h = _vp()
+        if hasattr(payload, "data_ptr"):
+            ptr, nbytes, on_dev = int(payload.data_ptr()), int(payload.numel() * payload.element_size()), 1
+            keep = None
+        else:
+            keep = _u8(payload)
+            ptr, nbytes, on_dev = keep.ctypes.data, keep.nbytes, 0
+        idbuf = C.create_string_buffer(bytes(nccl_id), 128) if nccl_id is not None else None
+        check(_lib.lib().satori_matrix_create_sharded(ctx.handle, ptr, nbytes, self.rows, self.columns, self.format,
+                                                      on_dev, rank, world, idbuf, C.byref(h)), "create_sharded")
+        del keep
+        self._h = h
+        b, e = C.c_int(), C.c_int()
+        check(_lib.lib().satori_matrix_sharded_info(h, C.byref(b), C.byref(e)), "sharded_info")
+        self.row_begin, self.row_end = b.value, e.value
+
+    @property
+    def handle(self):
+        if self._h is None or not self._h.value:
+            raise DisposedError(_lib.ERR_DISPOSED, "matrix is disposed")
+        return self._h
+
+    def execute(self, input, order: int = _lib.ORDER_BATCH, output: np.ndarray | None = None) -> np.ndarray:
+        x = _f32(input, self.columns, "input")
+        y = np.empty(self.rows, np.float32)
+        check(_lib.lib().satori_matrix_sharded_execute(self.handle, _ptr(x), _ptr(y), order), "sharded_execute")
+        return _commit(y, output)
+
+    def execute_device(self, dx: int, dy: int, order: int = _lib.ORDER_BATCH) -> None:
+        check(_lib.lib().satori_matrix_sharded_execute_device(self.handle, dx, dy, order), "sharded_execute_device")
+
+    def dispose(self) -> None:
+        if getattr(self, "_h", None) is not None and self._h.value:
+            _lib.lib().satori_matrix_sharded_destroy(self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.dispose()
+        except Exception:
+            pass
+
+
 class CudaMatrixFactory:
     """IQuantizedMatrixFactory over the GPU (the seam VulkanContext implements in the reference)."""
 

@@ -38,20 +38,10 @@
 #include "capi_internal.h"
 #include "common.cuh"
 #include "session_internal.h"
+#include "nccl_api.h"
 #include "xchg.cuh"
 
-using namespace satori;
-
-namespace {
-
-struct NcclApi {
-    void *lib = nullptr;
-    ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
-    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
-    ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
-    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
-    const char *(*GetErrorString)(ncclResult_t) = nullptr;
-};
+namespace satori {
 
 const NcclApi *nccl_api()
 {
@@ -74,6 +64,12 @@ int nccl_fail(const NcclApi *api, ncclResult_t r, const char *what)
 {
     return set_error(SATORI_ERR_CUDA, "%s: %s", what, api ? api->GetErrorString(r) : "NCCL unavailable");
 }
+
+}  // namespace satori
+
+using namespace satori;
+
+namespace {
 
 // Context blocks of rank i (query heads [i*qH/W, (i+1)*qH/W)) sit at pad + i*qmax*hd.
 __global__ void ctx_compact_kernel(const float *pad, float *ctx, int world, int q_heads, int head_dim, int qmax)

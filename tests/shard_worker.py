@@ -65,3 +65,53 @@ def run_silent_peer(rank: int, world: int, nccl_id: bytes, spec_kwargs: dict, se
     s.dispose()
     with open(out_path, "w") as f:
         f.write(repr(result))
+
+
+def sharded_matvec_cases():
+    """(rows, cols, format, order name, seed): an even Q4_0 split (the large GEMV shape), a Q8_0 split that
+    leaves a padded last slice, and Ternary2 in the AVX2 order."""
+    return [(11008, 4096, 1, "batch", 1), (1003, 1024, 0, "batch", 2), (1003, 1024, 0, "execute", 3),
+            (4096, 4096, 64, "execute", 4)]
+
+
+def case_inputs(rows: int, cols: int, fmt: int, seed: int):
+    """The same seeded payload and input on every rank (and in the parent that checks them)."""
+    rng = np.random.default_rng(seed)
+    if fmt >= 64:
+        from oracle import oracle
+        w = rng.standard_normal(rows * cols).astype(np.float32)
+        payload = oracle.t2_quantize(w, rows, cols, fmt)
+    else:
+        bb = 34 if fmt == 0 else 18
+        payload = rng.integers(0, 256, size=rows * (cols // 32) * bb, dtype=np.uint8)
+        scales = (rng.standard_normal(rows * (cols // 32)) * 0.05).astype(np.float16).view(np.uint16)
+        p2 = payload.reshape(-1, bb)
+        p2[:, 0] = scales & 0xFF
+        p2[:, 1] = scales >> 8
+    x = rng.standard_normal(cols).astype(np.float32)
+    return payload, x
+
+
+def run_sharded_matvec(rank: int, world: int, nccl_id: bytes, out_path: str) -> None:
+    """Every case through CudaShardedMatrix on this rank; saves the full gathered outputs."""
+    import satori_b200 as sat
+    from satori_b200 import _lib
+
+    ctx = sat.Context(rank)
+    outs = {}
+    for i, (rows, cols, fmt, order, seed) in enumerate(sharded_matvec_cases()):
+        payload, x = case_inputs(rows, cols, fmt, seed)
+
+        class Shape:
+            pass
+        shape = Shape()
+        shape.rows, shape.columns, shape.format = rows, cols, fmt
+        m = sat.CudaShardedMatrix(ctx, payload, shape, rank, world, nccl_id)
+        o = _lib.ORDER_BATCH if order == "batch" else _lib.ORDER_EXECUTE
+        outs[f"y{i}"] = m.execute(x, o)
+        outs[f"r{i}"] = np.array([m.row_begin, m.row_end], np.int32)
+        m.dispose()
+    tmp = out_path + ".part"
+    with open(tmp, "wb") as f:
+        np.savez(f, **outs)
+    os.replace(tmp, out_path)

@@ -14,6 +14,7 @@ import os
 import numpy as np
 import pytest
 
+from golden_util import bits_equal
 from model_util import synthetic_tensors
 
 pytestmark = pytest.mark.gpu
@@ -132,3 +133,32 @@ def test_silent_peer_times_out_and_latches(sat, tmp_path):
     r0 = ast.literal_eval(open(outs[0]).read())
     assert r0["first"] == sat._lib.ERR_TIMEOUT and r0["second"] == sat._lib.ERR_TIMEOUT
     assert 0.4 < r0["first_s"] < 30
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_matvec_equals_single_gpu_reference(sat, oracle_lib, tmp_path, world):
+    """The row-sharded large MatVec (satori_matrix_create_sharded): rank r holds rows [r*S, (r+1)*S) and
+    every rank ends with the full output after the NCCL all-gather; every value equals the oracle's
+    single-GPU result bit for bit (each row keeps the reference's operation order), including the padded
+    last slice of an uneven split."""
+    if _gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import shard_worker
+    nccl_id = sat.nccl_unique_id()
+    outs = [str(tmp_path / ("mv%d.npz" % r)) for r in range(world)]
+    codes = _spawn(shard_worker.run_sharded_matvec, [(r, world, nccl_id, outs[r]) for r in range(world)],
+                   {"NCCL_NVLS_ENABLE": "0"})
+    assert codes == [0] * world
+    res = [np.load(o) for o in outs]
+    for i, (rows, cols, fmt, order, seed) in enumerate(shard_worker.sharded_matvec_cases()):
+        payload, x = shard_worker.case_inputs(rows, cols, fmt, seed)
+        if fmt >= 64:
+            ref = oracle_lib.t2_matvec(payload, rows, cols, fmt, x, "avx2", threads=8)
+        else:
+            ref = oracle_lib.q_matvec(payload, rows, cols, fmt, x, order="batch" if order == "batch" else "avx2",
+                                      threads=8)
+        slice_ = -(-rows // world)
+        for r in range(world):
+            y = res[r][f"y{i}"]
+            assert list(res[r][f"r{i}"]) == [r * slice_, min(rows, (r + 1) * slice_)]
+            assert bits_equal(y, np.asarray(ref, np.float32)), (i, r)
