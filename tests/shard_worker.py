@@ -92,8 +92,9 @@ def case_inputs(rows: int, cols: int, fmt: int, seed: int):
     return payload, x
 
 
-def run_sharded_matvec(rank: int, world: int, nccl_id: bytes, out_path: str) -> None:
-    """Every case through CudaShardedMatrix on this rank; saves the full gathered outputs."""
+def run_sharded_matvec(rank: int, world: int, nccl_ids: list, out_path: str) -> None:
+    """Every case through CudaShardedMatrix on this rank (one NCCL id per case: an id serves one
+    communicator); saves the full gathered outputs."""
     import satori_b200 as sat
     from satori_b200 import _lib
 
@@ -106,7 +107,7 @@ def run_sharded_matvec(rank: int, world: int, nccl_id: bytes, out_path: str) -> 
             pass
         shape = Shape()
         shape.rows, shape.columns, shape.format = rows, cols, fmt
-        m = sat.CudaShardedMatrix(ctx, payload, shape, rank, world, nccl_id)
+        m = sat.CudaShardedMatrix(ctx, payload, shape, rank, world, nccl_ids[i])
         o = _lib.ORDER_BATCH if order == "batch" else _lib.ORDER_EXECUTE
         outs[f"y{i}"] = m.execute(x, o)
         outs[f"r{i}"] = np.array([m.row_begin, m.row_end], np.int32)

@@ -144,9 +144,9 @@ def test_sharded_matvec_equals_single_gpu_reference(sat, oracle_lib, tmp_path, w
     if _gpu_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import shard_worker
-    nccl_id = sat.nccl_unique_id()
+    ids = [sat.nccl_unique_id() for _ in shard_worker.sharded_matvec_cases()]
     outs = [str(tmp_path / ("mv%d.npz" % r)) for r in range(world)]
-    codes = _spawn(shard_worker.run_sharded_matvec, [(r, world, nccl_id, outs[r]) for r in range(world)],
+    codes = _spawn(shard_worker.run_sharded_matvec, [(r, world, ids, outs[r]) for r in range(world)],
                    {"NCCL_NVLS_ENABLE": "0"})
     assert codes == [0] * world
     res = [np.load(o) for o in outs]
