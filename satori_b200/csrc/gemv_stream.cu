@@ -116,23 +116,35 @@ __device__ __forceinline__ void st_compute(const StreamArgs &a, uint8_t *smem, i
     const int b = 2 * min(e, G::HALF - 1) + (PH ? 1 : 0);    // block index in the row (odd blocks: PH = 2)
     float4 xv[8];
     {
+        // The compute warps copy x (and the norm weights) into the ring, which holds no weights yet, with
+        // coalesced 16-byte loads (a lane loading its own block directly would make every warp load touch
+        // 32 lines); then each lane reads its block's 32 values.  Chunk q of block k sits at chunk
+        // q ^ ((k >> 1) & 7) of the block, so the eight lanes of a shared-memory wavefront (blocks two
+        // apart) read distinct banks.
+        float4 *xs = reinterpret_cast<float4 *>(const_cast<uint8_t *>(ring));
+        constexpr int NCH = NB * 8;
+        for (int i = cw * 32 + lane; i < NCH; i += CW * 32) {
+            const int k = i >> 3, dst = k * 8 + ((i & 7) ^ ((k >> 1) & 7));
+            xs[dst] = reinterpret_cast<const float4 *>(a.x)[i];
+            if (a.norm_w) xs[NCH + dst] = reinterpret_cast<const float4 *>(a.norm_w)[i];
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");   // the compute warps only
         const double scale = a.norm_w ? rms_scale(h.red, NB * 32, a.norm_eps) : 0.0;
-        const float4 *xb = reinterpret_cast<const float4 *>(a.x) + (size_t)b * 8;
+        const int sw = (b >> 1) & 7;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) xv[q] = xb[q];
+        for (int q = 0; q < 8; ++q) xv[q] = xs[b * 8 + (q ^ sw)];
         if (a.norm_w) {
-            const float4 *wb = reinterpret_cast<const float4 *>(a.norm_w) + (size_t)b * 8;
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-                const float4 w4 = wb[q];
+                const float4 w4 = xs[NCH + b * 8 + (q ^ sw)];
                 xv[q] = make_float4(rms_apply(xv[q].x, scale, w4.x), rms_apply(xv[q].y, scale, w4.y),
                                     rms_apply(xv[q].z, scale, w4.z), rms_apply(xv[q].w, scale, w4.w));
             }
         }
     }
-    // Release the weight copies only once this warp's activations are in registers: issued behind the
-    // copies, the activation loads would wait for the whole ring fill to reach the SM.  (Adding the 32
-    // values makes every load complete before the arrival.)
+    // Release the weight copies only once this warp's activations are in registers: the copies overwrite
+    // the staged activations, and issued earlier they would also delay the activation loads behind the
+    // ring fill.  (Adding the 32 values makes every load complete before the arrival.)
     {
         float all = 0.0f;
 #pragma unroll
@@ -398,6 +410,11 @@ DecodePlan plan_gemv_stream(const GemvArgs &a, int sm_count, size_t smem_limit)
     const int nst = (rc + v->rows_per_stage - 1) / v->rows_per_stage;
     int stages = (int)std::min<size_t>(kStMaxStages, (budget - fixed) / v->slot);
     stages = std::max(1, std::min(stages, nst));
+    // The ring first holds the staged activations (and norm weights): at least that much of it is needed.
+    const size_t staged = (size_t)v->nb * 128 * (a.norm_w ? 2 : 1);
+    while ((size_t)stages * v->slot < staged && stages < kStMaxStages && fixed + (size_t)(stages + 1) * v->slot <= budget)
+        ++stages;
+    if ((size_t)stages * v->slot < staged) return p;
     p.ok = 1;
     p.kind = 3;
     p.rc = rc;
