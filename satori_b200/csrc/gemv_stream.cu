@@ -121,8 +121,9 @@ __device__ __forceinline__ void st_compute(const StreamArgs &a, uint8_t *smem, i
         // 32 lines); then each lane reads its block's 32 values.  Chunk q of block k sits at chunk
         // q ^ ((k >> 1) & 7) of the block, so the eight lanes of a shared-memory wavefront (blocks two
         // apart) read distinct banks.
-        float4 *xs = reinterpret_cast<float4 *>(const_cast<uint8_t *>(ring));
         constexpr int NCH = NB * 8;
+        const int xslots = (NCH * 16 * (a.norm_w ? 2 : 1) + G::SLOT - 1) / G::SLOT;
+        float4 *xs = reinterpret_cast<float4 *>(const_cast<uint8_t *>(ring) + (size_t)(a.stages - xslots) * G::SLOT);
         for (int i = cw * 32 + lane; i < NCH; i += CW * 32) {
             const int k = i >> 3, dst = k * 8 + ((i & 7) ^ ((k >> 1) & 7));
             xs[dst] = reinterpret_cast<const float4 *>(a.x)[i];
@@ -240,12 +241,13 @@ __global__ void __launch_bounds__((CW + 2) * 32, MINB) gemv_stream_kernel(const 
         bulk_g2s(ring + (size_t)s * G::SLOT, a.payload + ((size_t)row0 + (size_t)i * G::R) * G::RB, bytes,
                  &h.full[s]);
     };
-    // Weights never depend on the previous kernel: the first stage starts moving into L2 before the
-    // programmatic-launch wait (only the first: requested together, the stages of every CTA would share
-    // the bandwidth and each CTA's first stage would land last); the copies into shared memory follow the
-    // activation loads.
-    if (producer && lane == 0 && nst > 0)
-        bulk_prefetch_l2(a.payload + (size_t)row0 * G::RB, (uint32_t)(min(G::R, nrows_cta) * G::RB));
+    // Weights never depend on the previous kernel: the stages whose slots lie below the activation
+    // staging area (the last slots of the ring) are requested before the programmatic-launch wait; the
+    // rest follow once every lane holds its activations.
+    const int xslots = (NB * 128 * (a.norm_w ? 2 : 1) + G::SLOT - 1) / G::SLOT;
+    const int early = max(0, min(nst, S - xslots));
+    if (producer && lane == 0)
+        for (int i = 0; i < early; ++i) issue(i, i);
     if (a.use_pdl) {
         pdl_launch_dependents();
         pdl_wait();
@@ -261,8 +263,11 @@ __global__ void __launch_bounds__((CW + 2) * 32, MINB) gemv_stream_kernel(const 
 
     if (producer) {
         if (lane != 0) return;
-        if (!st_wait(h.xready, 0, h, a.err)) return;
-        for (int i = 0; i < min(S, nst); ++i) issue(i, i);
+        if (!st_wait(h.xready, 0, h, a.err)) {
+            for (int k = 0; k < early; ++k) mbar_wait_bounded(&h.full[k], 0);   // copies land before exit
+            return;
+        }
+        for (int i = early; i < min(S, nst); ++i) issue(i, i);
         int i = S, s = 0;
         uint32_t par = 0;
         for (; i < nst; ++i) {
