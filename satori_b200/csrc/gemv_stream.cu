@@ -100,6 +100,51 @@ __device__ __forceinline__ bool st_wait(uint64_t *bar, uint32_t parity, const St
     return false;
 }
 
+// Where the compute warps stage x (and the norm weights): the last slots of the ring, which receive no
+// weights before every lane holds its activations.  Chunk q of block k sits at chunk q ^ ((k >> 1) & 7)
+// of the block, so the eight lanes of a shared-memory wavefront (blocks two apart) read distinct banks.
+template <int FMT, int NB, int CW, int RPW>
+__device__ __forceinline__ float4 *st_staged_x(const StreamArgs &a, const uint8_t *ring)
+{
+    using G = StGeo<FMT, NB, CW, RPW>;
+    const int xslots = (NB * 128 * (a.norm_w ? 2 : 1) + G::SLOT - 1) / G::SLOT;
+    return reinterpret_cast<float4 *>(const_cast<uint8_t *>(ring) + (size_t)(a.stages - xslots) * G::SLOT);
+}
+
+__device__ __forceinline__ int st_swz(int chunk)
+{
+    const int k = chunk >> 3;
+    return k * 8 + ((chunk & 7) ^ ((k >> 1) & 7));
+}
+
+// The compute warps copy x (and the norm weights) into the staging area with coalesced 16-byte loads:
+// a lane loading its own block directly would make every warp load touch 32 lines.
+template <int FMT, int NB, int CW, int RPW>
+__device__ __forceinline__ void st_stage_x(const StreamArgs &a, const uint8_t *ring, int ct)
+{
+    float4 *xs = st_staged_x<FMT, NB, CW, RPW>(a, ring);
+    constexpr int NCH = NB * 8;
+    for (int i = ct; i < NCH; i += CW * 32) {
+        const int dst = st_swz(i);
+        xs[dst] = reinterpret_cast<const float4 *>(a.x)[i];
+        if (a.norm_w) xs[NCH + dst] = reinterpret_cast<const float4 *>(a.norm_w)[i];
+    }
+}
+
+// rms_partial's sum (the same 256 strided partials and tree, so the same bits) over the staged copy of x.
+__device__ __forceinline__ void rms_partial_staged(const float4 *xs, int n, int tid, double *red)
+{
+    const float *f = reinterpret_cast<const float *>(xs);
+    double sum = 0;
+    for (int i = tid; i < n; i += 256) {
+        const float v = f[st_swz(i >> 2) * 4 + (i & 3)];
+        sum = __dadd_rn(sum, __dmul_rn((double)v, (double)v));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum = __dadd_rn(sum, __shfl_xor_sync(0xFFFFFFFFu, sum, o));
+    if ((tid & 31) == 0) red[tid >> 5] = sum;
+}
+
 // Compute warp `cw` (0-based) for phase PH.
 template <int FMT, int NB, int CW, int RPW, int PH>
 __device__ __forceinline__ void st_compute(const StreamArgs &a, uint8_t *smem, int cw, int lane, int nrows_cta,
@@ -116,19 +161,10 @@ __device__ __forceinline__ void st_compute(const StreamArgs &a, uint8_t *smem, i
     const int b = 2 * min(e, G::HALF - 1) + (PH ? 1 : 0);    // block index in the row (odd blocks: PH = 2)
     float4 xv[8];
     {
-        // The compute warps copy x (and the norm weights) into the ring, which holds no weights yet, with
-        // coalesced 16-byte loads (a lane loading its own block directly would make every warp load touch
-        // 32 lines); then each lane reads its block's 32 values.  Chunk q of block k sits at chunk
-        // q ^ ((k >> 1) & 7) of the block, so the eight lanes of a shared-memory wavefront (blocks two
-        // apart) read distinct banks.
+        // x (and the norm weights) were staged into the ring by the compute warps (st_stage_x); each lane
+        // reads its block's 32 values from there.
         constexpr int NCH = NB * 8;
-        const int xslots = (NCH * 16 * (a.norm_w ? 2 : 1) + G::SLOT - 1) / G::SLOT;
-        float4 *xs = reinterpret_cast<float4 *>(const_cast<uint8_t *>(ring) + (size_t)(a.stages - xslots) * G::SLOT);
-        for (int i = cw * 32 + lane; i < NCH; i += CW * 32) {
-            const int k = i >> 3, dst = k * 8 + ((i & 7) ^ ((k >> 1) & 7));
-            xs[dst] = reinterpret_cast<const float4 *>(a.x)[i];
-            if (a.norm_w) xs[NCH + dst] = reinterpret_cast<const float4 *>(a.norm_w)[i];
-        }
+        const float4 *xs = st_staged_x<FMT, NB, CW, RPW>(a, ring);
         asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");   // the compute warps only
         const double scale = a.norm_w ? rms_scale(h.red, NB * 32, a.norm_eps) : 0.0;
         const int sw = (b >> 1) & 7;
@@ -256,8 +292,11 @@ __global__ void __launch_bounds__((CW + 2) * 32, MINB) gemv_stream_kernel(const 
         if (tid == 0) xwait_peers(a.xw, a.err);
         __syncthreads();
     }
+    if (warp >= 1 && warp <= CW) st_stage_x<FMT, NB, CW, RPW>(a, ring, tid - 32);
     if (a.norm_w) {
-        if (tid < 256) rms_partial(a.x, NB * 32, tid, h.red);
+        // The norm's sum of squares reads the staged copy (one pass over global memory instead of two).
+        __syncthreads();
+        if (tid < 256) rms_partial_staged(st_staged_x<FMT, NB, CW, RPW>(a, ring), NB * 32, tid, h.red);
         __syncthreads();
     }
 
