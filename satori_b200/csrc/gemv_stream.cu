@@ -100,6 +100,14 @@ __device__ __forceinline__ bool st_wait(uint64_t *bar, uint32_t parity, const St
     return false;
 }
 
+// The fused RmsNorm of x exists for the hidden widths only (the inputs of q/k/v and gate/up); the wide
+// variants (ffn widths, inputs of ffn_down) leave it out and keep their registers for the block terms.
+template <int NB>
+__device__ __forceinline__ bool st_norm(const StreamArgs &a)
+{
+    return NB <= 128 && a.norm_w != nullptr;
+}
+
 // Where the compute warps stage x (and the norm weights): the last slots of the ring, which receive no
 // weights before every lane holds its activations.  Chunk q of block k sits at chunk q ^ ((k >> 1) & 7)
 // of the block, so the eight lanes of a shared-memory wavefront (blocks two apart) read distinct banks.
@@ -107,7 +115,7 @@ template <int FMT, int NB, int CW, int RPW>
 __device__ __forceinline__ float4 *st_staged_x(const StreamArgs &a, const uint8_t *ring)
 {
     using G = StGeo<FMT, NB, CW, RPW>;
-    const int xslots = (NB * 128 * (a.norm_w ? 2 : 1) + G::SLOT - 1) / G::SLOT;
+    const int xslots = (NB * 128 * (st_norm<NB>(a) ? 2 : 1) + G::SLOT - 1) / G::SLOT;
     return reinterpret_cast<float4 *>(const_cast<uint8_t *>(ring) + (size_t)(a.stages - xslots) * G::SLOT);
 }
 
@@ -127,7 +135,7 @@ __device__ __forceinline__ void st_stage_x(const StreamArgs &a, const uint8_t *r
     for (int i = ct; i < NCH; i += CW * 32) {
         const int dst = st_swz(i);
         xs[dst] = reinterpret_cast<const float4 *>(a.x)[i];
-        if (a.norm_w) xs[NCH + dst] = reinterpret_cast<const float4 *>(a.norm_w)[i];
+        if (st_norm<NB>(a)) xs[NCH + dst] = reinterpret_cast<const float4 *>(a.norm_w)[i];
     }
 }
 
@@ -166,11 +174,11 @@ __device__ __forceinline__ void st_compute(const StreamArgs &a, uint8_t *smem, i
         constexpr int NCH = NB * 8;
         const float4 *xs = st_staged_x<FMT, NB, CW, RPW>(a, ring);
         asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");   // the compute warps only
-        const double scale = a.norm_w ? rms_scale(h.red, NB * 32, a.norm_eps) : 0.0;
+        const double scale = st_norm<NB>(a) ? rms_scale(h.red, NB * 32, a.norm_eps) : 0.0;
         const int sw = (b >> 1) & 7;
 #pragma unroll
         for (int q = 0; q < 8; ++q) xv[q] = xs[b * 8 + (q ^ sw)];
-        if (a.norm_w) {
+        if (st_norm<NB>(a)) {
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
                 const float4 w4 = xs[NCH + b * 8 + (q ^ sw)];
@@ -280,7 +288,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, MINB) gemv_stream_kernel(const 
     // Weights never depend on the previous kernel: the stages whose slots lie below the activation
     // staging area (the last slots of the ring) are requested before the programmatic-launch wait; the
     // rest follow once every lane holds its activations.
-    const int xslots = (NB * 128 * (a.norm_w ? 2 : 1) + G::SLOT - 1) / G::SLOT;
+    const int xslots = (NB * 128 * (st_norm<NB>(a) ? 2 : 1) + G::SLOT - 1) / G::SLOT;
     const int early = max(0, min(nst, S - xslots));
     if (producer && lane == 0)
         for (int i = 0; i < early; ++i) issue(i, i);
@@ -293,7 +301,7 @@ __global__ void __launch_bounds__((CW + 2) * 32, MINB) gemv_stream_kernel(const 
         __syncthreads();
     }
     if (warp >= 1 && warp <= CW) st_stage_x<FMT, NB, CW, RPW>(a, ring, tid - 32);
-    if (a.norm_w) {
+    if (st_norm<NB>(a)) {
         // The norm's sum of squares reads the staged copy (one pass over global memory instead of two).
         __syncthreads();
         if (tid < 256) rms_partial_staged(st_staged_x<FMT, NB, CW, RPW>(a, ring), NB * 32, tid, h.red);
@@ -455,6 +463,7 @@ DecodePlan plan_gemv_stream(const GemvArgs &a, int sm_count, size_t smem_limit)
     int stages = (int)std::min<size_t>(kStMaxStages, (budget - fixed) / v->slot);
     stages = std::max(1, std::min(stages, nst));
     // The ring first holds the staged activations (and norm weights): at least that much of it is needed.
+    if (a.norm_w && v->nb > 128) return p;                  // no fused norm in the wide variants
     const size_t staged = (size_t)v->nb * 128 * (a.norm_w ? 2 : 1);
     while ((size_t)stages * v->slot < staged && stages < kStMaxStages && fixed + (size_t)(stages + 1) * v->slot <= budget)
         ++stages;
