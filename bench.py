@@ -692,6 +692,8 @@ def bench_matvec_sharded(args, rank, world, local):
         for _ in range(args.steps):
             with torch.cuda.stream(ext):
                 flush.sum(dtype=torch.int64)
+            torch.cuda.synchronize()
+            dist_barrier(world)           # every rank enters the timed call together (no flush skew inside)
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record(ext)
             m.execute_device(x.data_ptr(), y.data_ptr(), _lib.ORDER_BATCH)
