@@ -9,7 +9,7 @@ from ._lib import (ArgumentError, ContextFullError, DeviceError, DisposedError, 
 from .core import (AttentionCache, BlockQuantization, Context, CudaMatrixFactory, CudaQuantizedMatrix, CudaShardedMatrix,
                    MappedTernary2Matrix, QuantizedMatrixShape, Ternary2Matrix, Ternary2MatVec, TernaryBitplaneMatrix,
                    TernaryBitplaneMatVec, TransformerOps,
-                   default_context, stq2_header, stq2_read_header, ternary2_byte_length)
+                   default_context, sharded_matrix_rows, stq2_header, stq2_read_header, ternary2_byte_length)
 from .gguf import GgufFile, GgufMetadata, GgufTensor, open_stq2, session_from_gguf
 from .model import (CudaDenseSession, ModelSpec, broadcast_nccl_id, nccl_unique_id, qwen2_1_5b, qwen2_7b,
                     shard_ranges, tiny)
@@ -21,7 +21,7 @@ __all__ = [
     "CudaShardedMatrix",
     "MappedTernary2Matrix", "QuantizedMatrixShape", "Ternary2Matrix", "Ternary2MatVec", "TernaryBitplaneMatrix",
     "TernaryBitplaneMatVec", "TransformerOps",
-    "default_context", "stq2_header", "stq2_read_header", "ternary2_byte_length", "CudaDenseSession", "ModelSpec",
+    "default_context", "sharded_matrix_rows", "stq2_header", "stq2_read_header", "ternary2_byte_length", "CudaDenseSession", "ModelSpec",
     "qwen2_1_5b", "qwen2_7b", "tiny", "nccl_unique_id", "broadcast_nccl_id", "shard_ranges",
     "GgufFile", "GgufMetadata", "GgufTensor", "open_stq2", "session_from_gguf",
 ]

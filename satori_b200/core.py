@@ -257,6 +257,18 @@ class CudaQuantizedMatrix:
             pass
 
 
+def sharded_matrix_rows(rows: int, rank: int, world: int) -> tuple:
+    """Rows [begin, end) that rank `rank` of `world` holds in a row-sharded matrix (the rule of
+    satori_matrix_create_sharded): blocks of S = ceil(rows / world) rows, the last one shorter; every rank
+    must receive at least one row."""
+    if world < 1 or not 0 <= rank < world or rows <= 0:
+        raise ArgumentError(_lib.ERR_ARGUMENT, f"bad rank {rank} / world {world} / rows {rows}")
+    s = -(-rows // world)
+    if s * (world - 1) >= rows:
+        raise _lib.NotSupportedError(_lib.ERR_NOT_SUPPORTED, f"{rows} rows leave rank {world - 1} of {world} without rows")
+    return rank * s, min(rows, (rank + 1) * s)
+
+
 class CudaShardedMatrix:
     """One large MatVec split by rows over the GPUs of a node (one process per GPU): rank r holds rows
     [r*S, min((r+1)*S, rows)), S = ceil(rows / world), computes them with the single-GPU kernels (each row
