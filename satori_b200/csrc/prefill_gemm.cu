@@ -9,7 +9,7 @@
 // operand is exact and every product exact:
 //  * a weight w = d * q (fp16 scale times a 4- or 8-bit code) has at most 15 (Q4_0) or 19 (Q8_0)
 //    significant bits, so it is exactly w1 + w2 (+ w3) with bf16 parts w_i (8 bits each, FP32's range);
-//  * an activation x is x1 + x2 + x3 with bf16 parts, to within 2^-24 |x|;
+//  * an activation x is x1 + x2 + x3 with bf16 parts, to within 2^-27 |x|;
 //  * the cross products w_i * x_j with weight above 2^-24 go through kind::f16 MMAs (bf16 x bf16 ->
 //    exact FP32 product) into one FP32 accumulator in tensor memory: 5 MMAs per K step for Q4_0, 6 for
 //    Q8_0.
@@ -17,10 +17,11 @@
 // sum |w x|), which the prefill tests bound.
 //
 // One CTA computes a 128-row x N-position tile (N = positions rounded up to 16, at most 128):
-//  * warps 0-3 (one warpgroup; thread t = row t of the tile) read the tile's Q8_0/Q4_0 blocks 64 columns
-//    at a time, decode w exactly, split it and store the bf16 parts in the canonical K-major layout
-//    (8-row x 16-byte core matrices, no swizzle); after the last K step they read the accumulator back
-//    with tcgen05.ld (warp w owns TMEM lanes 32w..32w+31) and write Y;
+//  * warps 0-3 (one warpgroup; thread t = row t of the tile) stage their row's Q8_0/Q4_0 bytes four
+//    64-column steps ahead with cp.async, decode w exactly (byte-permute + FP32x2 FMA), split it with
+//    packed bf16x2 conversions and store the parts in the canonical K-major layout (8-row x 16-byte core
+//    matrices, no swizzle); after the last K step they read the accumulator back with tcgen05.ld (warp w
+//    owns TMEM lanes 32w..32w+31) and write Y;
 //  * warp 4 allocates the tensor memory, streams the pre-split activation tiles with 1-D bulk copies,
 //    and one elected thread issues the MMAs and commits them to an mbarrier that frees the stage.
 // Two stages; every wait is bounded, and on an expired wait the CTA still drains its MMAs and frees
