@@ -993,6 +993,10 @@ bool launch_stream(const AttnArgs &a, AttnParams &p, int gmax, int sm_count, cud
     }
     // About one CTA per SM (each keeps ~64 KB in flight); never more splits than the scratch holds.
     p.nsplit = std::max(1, std::min(p.nsplit, (sm_count + units * p.batch - 1) / (units * p.batch)));
+    // At least 128 tokens per split (two 8-token tiles per compute warp, so the CTA-level merge of the
+    // warps' states is shared by twice the work), unless that would leave fewer than about half as many
+    // CTAs as SMs: short contexts keep their 64-token splits.
+    p.nsplit = std::max(1, std::min(p.nsplit, std::max(cap / 128, (sm_count + 2 * units - 1) / (2 * units))));
     const cudaError_t e = opt_in_smem(reinterpret_cast<const void *>(attn_stream_kernel), kStreamSmem);
     if (e != cudaSuccess) {
         *err = e;
