@@ -438,6 +438,82 @@ def prefill_record(sess, spec, P, stream_ctx, repeats=3):
                      "the rest as the decode step"}
 
 
+def kernel_matvec_kquant(ctx, stream, fmt, rows, cols, **kw):
+    """GGUF Q4_K / Q6_K MatVec in the decode (ExecuteBatch) order: random blocks with finite fp16 scales
+    (timing only: the block term's cost does not depend on the values), rotating copies > 4x L2."""
+    import torch
+
+    import satori_b200 as sat
+    from satori_b200 import _lib
+    bb = 144 if fmt == _lib.Q4_K else 210
+    nblk = rows * (cols // 256)
+    rng = np.random.default_rng(fmt)
+    host = rng.integers(0, 256, size=(nblk, bb), dtype=np.uint8)
+    sc = (rng.standard_normal((nblk, 2)) * 0.01).astype(np.float16).view(np.uint16)
+    if fmt == _lib.Q4_K:
+        host[:, 0], host[:, 1], host[:, 2], host[:, 3] = sc[:, 0] & 0xFF, sc[:, 0] >> 8, sc[:, 1] & 0xFF, sc[:, 1] >> 8
+    else:
+        host[:, 208], host[:, 209] = sc[:, 0] & 0xFF, sc[:, 0] >> 8
+    nbytes = host.size
+    copies = max(1, int(math.ceil(4 * 126e6 / nbytes)))
+    first = sat.CudaQuantizedMatrix(ctx, host.reshape(-1), rows, cols, fmt)
+    mats = [first] + [sat.CudaQuantizedMatrix.from_device(ctx, first.device_payload, nbytes, rows, cols, fmt)
+                      for _ in range(copies - 1)]
+    x = torch.randn(cols, generator=torch.Generator(device="cuda").manual_seed(3), device="cuda")
+    y = torch.empty(rows, device="cuda")
+    torch.cuda.synchronize()
+    ctx.set_stream(stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        mats[0].execute_device(x.data_ptr(), y.data_ptr(), 1, _lib.ORDER_BATCH)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for m in mats:
+            m.execute_device(x.data_ptr(), y.data_ptr(), 1, _lib.ORDER_BATCH)
+    torch.cuda.synchronize()
+    ms = repeat_regions(graph.replay, stream, copies, **kw)
+    ctx.set_stream(None)
+    del graph
+    for m in mats:
+        m.dispose()
+    return nbytes, ms, copies
+
+
+def kernel_bitplane(ctx, stream, n, bs, **kw):
+    """STB1 bitplane n x n MatVec (TernaryBitplaneAvx2Kernel order) from the same N(0,1) Ternary2 matrix as
+    configs[0], rotating copies > 4x L2."""
+    import torch
+
+    import satori_b200 as sat
+    from satori_b200 import _lib
+    from satori_b200.core import ternary2_byte_length
+    nbytes = ternary2_byte_length(n, n, bs)
+    copies = max(4, int(np.ceil(4 * 126e6 / nbytes)))
+    w = np.random.default_rng(1).standard_normal(n * n).astype(np.float32)
+    tb = sat.TernaryBitplaneMatrix.from_ternary2(sat.Ternary2Matrix.quantize(w, n, n, bs, ctx=ctx))
+    fmt = {64: _lib.TB_64, 128: _lib.TB_128, 256: _lib.TB_256}[bs]
+    mats = [tb.device] + [sat.CudaQuantizedMatrix.from_device(ctx, tb.device.device_payload, nbytes, n, n, fmt)
+                          for _ in range(copies - 1)]
+    x = torch.randn(n, device="cuda")
+    y = torch.empty(n, device="cuda")
+    torch.cuda.synchronize()
+    ctx.set_stream(stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        mats[0].execute_device(x.data_ptr(), y.data_ptr(), 1, _lib.ORDER_EXECUTE)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for m in mats:
+            m.execute_device(x.data_ptr(), y.data_ptr(), 1, _lib.ORDER_EXECUTE)
+    torch.cuda.synchronize()
+    ms = repeat_regions(graph.replay, stream, copies, **kw)
+    ctx.set_stream(None)
+    del graph
+    for m in mats[1:]:
+        m.dispose()
+    return nbytes, ms, copies
+
+
 def kernels_record(ctx, min_region_s=0.5, repeats=5):
     import torch
     peak, kind = _peaks()
@@ -462,6 +538,16 @@ def kernels_record(ctx, min_region_s=0.5, repeats=5):
         out[f"ternary2_4096x4096_bs{bs}"] = stats_record(b, ms, peak, kind,
                                                          {"workload": f"configs[0] bs{bs}", "copies": copies,
                                                           "order": "Ternary2Avx2Kernel, bit-exact"})
+    from satori_b200 import _lib
+    for fmt, label in ((_lib.Q4_K, "q4_k"), (_lib.Q6_K, "q6_k")):
+        b, ms, copies = kernel_matvec_kquant(ctx, stream, fmt, 4096, 4096, **kw)
+        out[f"matvec_{label}_4096x4096"] = stats_record(
+            b, ms, peak, kind, {"workload": "GGUF K-quant, configs[1] Q8_0 shape", "copies": copies,
+                                "order": "ExecuteBatch with Q8_K activations (decode), bit-exact"})
+    b, ms, copies = kernel_bitplane(ctx, stream, 4096, 128, **kw)
+    out["bitplane_stb1_4096x4096_bs128"] = stats_record(
+        b, ms, peak, kind, {"workload": "configs[0] shape, STB1 layout", "copies": copies,
+                            "order": "TernaryBitplaneAvx2Kernel, bit-exact"})
     for name, fmt, rows, cols in PREFILL_SHAPES:
         out[f"prefill_gemm_{name}"] = kernel_prefill_gemm(ctx, stream, name, fmt, rows, cols, **kw)
     return out
@@ -657,7 +743,7 @@ def bench_decode(args, rank, world, local, spec, with_kernels: bool):
         res["prefill"] = prefill_record(sess, spec, P, ctx)
     sess.dispose()
     if with_kernels and rank == 0 and world == 1:
-        res["kernels"] = kernels_record(ctx)
+        res["kernels"] = kernels_record(ctx, min_region_s=args.region, repeats=args.repeats)
     if rank == 0 and world == 1 and host is not None and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_decode(spec, host, P)
     return res
