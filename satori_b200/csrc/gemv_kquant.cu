@@ -127,6 +127,8 @@ struct KBatchArgs {
     const float *bias;
     float *residual;
     int use_pdl;
+    int stage;                 // 1: each warp copies its row into shared memory first (coalesced)
+    int stage_stride;          // bytes of shared memory per warp's row copy (a multiple of 16, with slack)
 };
 
 // The exact integer product(s) of one (row, block) and its FP32 term; `rec` = the Q8_K record.
@@ -200,16 +202,29 @@ __global__ void __launch_bounds__(kKWarps * 32) kq_batch_kernel(const KBatchArgs
     extern __shared__ __align__(16) uint8_t kq_smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nb = a.cols / 256;
+    constexpr int BB = FMT == SATORI_Q4_K ? 144 : 210;
+    const int row = blockIdx.x * kKWarps + warp;
+    const uint8_t *rowp = a.payload + (size_t)min(row, a.rows - 1) * nb * BB;
+    // The weights do not depend on the previous kernel: each warp's row starts moving into shared memory
+    // (16-byte asynchronous copies, coalesced; a lane reading its own block would make every warp load
+    // touch 32 lines) before the programmatic-launch wait, and lands while x is quantized.
+    uint8_t *staged = kq_smem + (size_t)nb * kKRecord + (size_t)warp * a.stage_stride;
+    if (a.stage && row < a.rows) {
+        for (int i = lane; i < nb * BB / 16; i += 32)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(staged + 16 * i)),
+                         "l"(rowp + 16 * i)
+                         : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     if (a.use_pdl) {
         pdl_launch_dependents();
         pdl_wait();
     }
     for (int b = warp; b < nb; b += kKWarps) q8k_quantize_warp(a.x + b * 256, kq_smem + b * kKRecord, lane);
+    if (a.stage) asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
-    constexpr int BB = FMT == SATORI_Q4_K ? 144 : 210;
-    const int row = blockIdx.x * kKWarps + warp;
     if (row >= a.rows) return;
-    const uint8_t *rowp = a.payload + (size_t)row * nb * BB;
+    if (a.stage) rowp = staged;
     constexpr int kMaxPerLane = 4;                               // up to 128 blocks (32768 columns)
     float t[kMaxPerLane];
     bool live[kMaxPerLane];
@@ -378,8 +393,20 @@ cudaError_t launch_kq_gemv(const GemvArgs &a, cudaStream_t stream)
     if (!is_kquant(a.format) || a.cols % 256 != 0 || a.cols > 32768) return cudaErrorInvalidValue;
     if (a.order == SATORI_ORDER_BATCH) {
         if (a.positions != 1) return cudaErrorInvalidValue;
-        KBatchArgs k = {a.payload, a.rows, a.cols, a.x, a.y, a.epilogue, a.bias, a.residual, a.use_pdl};
-        const size_t smem = (size_t)(a.cols / 256) * kKRecord;
+        KBatchArgs k = {a.payload, a.rows, a.cols, a.x, a.y, a.epilogue, a.bias, a.residual, a.use_pdl, 0, 0};
+        const int nb = a.cols / 256, bb = a.format == SATORI_Q4_K ? 144 : 210;
+        size_t smem = (size_t)nb * kKRecord;
+        // Rows are staged through shared memory when each row starts on a 16-byte boundary and the copies fit.
+        // Each copy is followed by 16 bytes of slack: a Q6_K term reads its 210-byte block as 53 words, and
+        // for a block at an odd 2-byte offset the last word reaches up to 6 bytes past the block (in global
+        // memory the payload's padding covers the same reads).
+        const size_t row_bytes = (size_t)nb * bb, stride = row_bytes + 16;
+        if (row_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(a.payload) & 15) == 0 &&
+            smem + kKWarps * stride <= 96 * 1024) {
+            k.stage = 1;
+            k.stage_stride = (int)stride;
+            smem += kKWarps * stride;
+        }
         auto kern = a.format == SATORI_Q4_K ? kq_batch_kernel<SATORI_Q4_K> : kq_batch_kernel<SATORI_Q6_K>;
         const cudaError_t e = opt_in_smem(reinterpret_cast<const void *>(kern), smem);
         if (e != cudaSuccess) return e;
