@@ -131,69 +131,95 @@ struct KBatchArgs {
     int stage_stride;          // bytes of shared memory per warp's row copy (a multiple of 16, with slack)
 };
 
-// The exact integer product(s) of one (row, block) and its FP32 term; `rec` = the Q8_K record.
+// Half `h` of one (row, block) product: the exact integer sums of sub-blocks 4h..4h+3 (Q4_K) or groups
+// 8h..8h+7 (Q6_K), which two lanes add together before one of them forms the FP32 term (k_term); integer
+// sums do not depend on their order, so the term is the reference's bit for bit.  `rec` = the Q8_K record.
 template <int FMT>
-__device__ __forceinline__ float k_block_term(const uint8_t *blk, const uint8_t *rec, bool &skip)
+__device__ __forceinline__ void k_block_half(const uint8_t *blk, const uint8_t *rec, int h, int &isum, int &mins)
 {
-    const float as = *reinterpret_cast<const float *>(rec + 288);
-    skip = as == 0.0f;
     const uint32_t *codes = reinterpret_cast<const uint32_t *>(rec);
     const int16_t *sums = reinterpret_cast<const int16_t *>(rec + 256);
+    isum = 0;
+    mins = 0;
     if (FMT == SATORI_Q4_K) {
+        // Words 0..3: d, dmin and the 12 scale bytes; then this half's 64 code bytes (words 4 + 16h ..).
         const uint4 *b4 = reinterpret_cast<const uint4 *>(blk);
-        uint32_t w[36];
-#pragma unroll
-        for (int k = 0; k < 9; ++k) {
-            const uint4 t = b4[k];
-            w[4 * k] = t.x;
-            w[4 * k + 1] = t.y;
-            w[4 * k + 2] = t.z;
-            w[4 * k + 3] = t.w;
+        uint32_t hw[4], qs[16];
+        {
+            const uint4 t = b4[0];
+            hw[0] = t.x, hw[1] = t.y, hw[2] = t.z, hw[3] = t.w;
         }
-        const uint8_t *bytes = reinterpret_cast<const uint8_t *>(w);
-        const float d = half_bits_to_float(w[0]), dmin = half_bits_to_float(w[0] >> 16);
-        int isum = 0, mins = 0;
 #pragma unroll
-        for (int sub = 0; sub < 8; ++sub) {
+        for (int k = 0; k < 4; ++k) {
+            const uint4 t = b4[1 + 4 * h + k];
+            qs[4 * k] = t.x, qs[4 * k + 1] = t.y, qs[4 * k + 2] = t.z, qs[4 * k + 3] = t.w;
+        }
+        // Scale byte n of the 12 (bytes 4 + n of the block), picked by shifts and selects (no local array:
+        // the half h is a runtime value).
+        auto sb = [&](int n) -> int {
+            const uint32_t wd = n < 4 ? hw[1] : (n < 8 ? hw[2] : hw[3]);
+            return (int)((wd >> (8 * (n & 3))) & 0xFFu);
+        };
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const int sub = 4 * h + s;
             int sc, mn;
-            q4k_scale_min(sub, bytes + 4, sc, mn);
+            if (h == 0) {                       // Q4KCodec.GetScaleMin (Q4KCodec.cs:24-37), j < 4
+                sc = sb(s) & 63;
+                mn = sb(s + 4) & 63;
+            } else {                            // j = 4 + s
+                sc = (sb(s + 8) & 0xF) | ((sb(s) >> 6) << 4);
+                mn = (sb(s + 8) >> 4) | ((sb(s + 4) >> 6) << 4);
+            }
             int acc = 0;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
-                const uint32_t q = w[4 + (sub >> 1) * 8 + k];           // qs bytes (sub/2)*32 + 4k
-                const uint32_t nib = (sub & 1) ? (q >> 4) & 0x0F0F0F0Fu : q & 0x0F0F0F0Fu;
+                const uint32_t q = qs[(s >> 1) * 8 + k];              // qs bytes (sub/2)*32 + 4k
+                const uint32_t nib = (s & 1) ? (q >> 4) & 0x0F0F0F0Fu : q & 0x0F0F0F0Fu;
                 acc = dp4a_us(nib, codes[sub * 8 + k], acc);
             }
             isum += sc * acc;
             mins += mn * ((int)sums[2 * sub] + (int)sums[2 * sub + 1]);
         }
-        const float da = fmul(d, as), ma = fmul(dmin, as);
-        return __fsub_rn(fmul(da, __int2float_rn(isum)), fmul(ma, __int2float_rn(mins)));
     } else {
-        uint32_t w[53];
+        // This half's low bits (words 16h ..), high bits (words 32 + 8h ..) and 8 scales (bytes 192 + 8h).
+        uint32_t ql[16], qh[8], sw[2];
 #pragma unroll
-        for (int k = 0; k < 53; ++k) w[k] = ld_u32_any(blk + 4 * k);
-        const uint8_t *bytes = reinterpret_cast<const uint8_t *>(w);
-        const float d = h2f(bytes + 208);
-        const int8_t *scales = reinterpret_cast<const int8_t *>(bytes + 192);
-        int isum = 0;
+        for (int j = 0; j < 16; ++j) ql[j] = ld_u32_any(blk + 4 * (16 * h + j));
 #pragma unroll
-        for (int g = 0; g < 16; ++g) {                          // 16-weight group g = sub-block g
-            const int half = g >> 3, k = (g & 7) >> 1, l0 = (g & 1) * 16;
+        for (int j = 0; j < 8; ++j) qh[j] = ld_u32_any(blk + 4 * (32 + 8 * h + j));
+        sw[0] = ld_u32_any(blk + 192 + 8 * h);
+        sw[1] = ld_u32_any(blk + 196 + 8 * h);
+        const uint32_t *hcodes = codes + 32 * h;
+#pragma unroll
+        for (int gg = 0; gg < 8; ++gg) {                         // group g = 8h + gg = sub-block g
+            const int k = gg >> 1, l0 = (gg & 1) * 16;
             int acc = 0;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int l = l0 + 4 * i;
-                const uint32_t qlw = w[(half * 64 + (k & 1) * 32 + l) >> 2];
-                const uint32_t qhw = w[(128 + half * 32 + l) >> 2];
+                const uint32_t qlw = ql[((k & 1) * 32 + l) >> 2];
+                const uint32_t qhw = qh[l >> 2];
                 const uint32_t nib = k < 2 ? qlw & 0x0F0F0F0Fu : (qlw >> 4) & 0x0F0F0F0Fu;
                 const uint32_t q = nib | (((qhw >> (2 * k)) & 0x03030303u) << 4);
-                acc = dp4a_us(q, codes[(half * 128 + 32 * k + l) >> 2], acc);
+                acc = dp4a_us(q, hcodes[(32 * k + l) >> 2], acc);
             }
-            isum += (int)scales[g] * (acc - 32 * (int)sums[g]);
+            const int scale = (int)(int8_t)((sw[gg >> 2] >> (8 * (gg & 3))) & 0xFFu);
+            isum += scale * (acc - 32 * (int)sums[8 * h + gg]);
         }
-        return fmul(fmul(as, d), __int2float_rn(isum));
     }
+}
+
+// The FP32 term of a block from its whole integer sums (the reference's combine order).
+template <int FMT>
+__device__ __forceinline__ float k_term(const uint8_t *blk, float as, int isum, int mins)
+{
+    if (FMT == SATORI_Q4_K) {
+        const float d = h2f(blk), dmin = h2f(blk + 2);
+        const float da = fmul(d, as), ma = fmul(dmin, as);
+        return __fsub_rn(fmul(da, __int2float_rn(isum)), fmul(ma, __int2float_rn(mins)));
+    }
+    return fmul(fmul(as, h2f(blk + 208)), __int2float_rn(isum));
 }
 
 template <int FMT>
@@ -225,32 +251,41 @@ __global__ void __launch_bounds__(kKWarps * 32) kq_batch_kernel(const KBatchArgs
     __syncthreads();
     if (row >= a.rows) return;
     if (a.stage) rowp = staged;
-    constexpr int kMaxPerLane = 4;                               // up to 128 blocks (32768 columns)
+    // Lanes 2j and 2j+1 share block j of each pass of 16 (one half each), so a 16-block row uses the
+    // whole warp; the even lane holds the block's term.
+    constexpr int kMaxPerLane = 8;                               // up to 128 blocks (32768 columns)
     float t[kMaxPerLane];
     bool live[kMaxPerLane];
+    const int h = lane & 1;
 #pragma unroll
     for (int i = 0; i < kMaxPerLane; ++i) {
-        const int b = lane + 32 * i;
         live[i] = false;
         t[i] = 0.0f;
-        if (b < nb) {
-            bool skip;
-            t[i] = k_block_term<FMT>(rowp + (size_t)b * BB, kq_smem + b * kKRecord, skip);
-            live[i] = !skip;
+        if (16 * i < nb) {                                       // warp-uniform: the shuffles see every lane
+            const int b = (lane >> 1) + 16 * i;
+            const int bc = min(b, nb - 1);                       // lanes past the row repeat its last block
+            const uint8_t *blk = rowp + (size_t)bc * BB, *rec = kq_smem + bc * kKRecord;
+            int isum, mins;
+            k_block_half<FMT>(blk, rec, h, isum, mins);
+            isum += __shfl_xor_sync(0xFFFFFFFFu, isum, 1);
+            mins += __shfl_xor_sync(0xFFFFFFFFu, mins, 1);
+            const float as = *reinterpret_cast<const float *>(rec + 288);
+            if (b < nb && as != 0.0f) {                          // an all-zero activation block adds nothing
+                t[i] = k_term<FMT>(blk, as, isum, mins);
+                live[i] = true;
+            }
         }
     }
-    // acc[row] += term, block by block (skipped blocks add nothing).
+    // acc[row] += term, block by block (skipped blocks add nothing): block 16i + j is t[i] of lane 2j.
     float acc = 0.0f;
-    for (int b = 0; b < nb; ++b) {
-        float v = 0.0f;
-        bool on = false;
 #pragma unroll
-        for (int i = 0; i < kMaxPerLane; ++i)
-            if ((b >> 5) == i) {
-                v = __shfl_sync(0xFFFFFFFFu, t[i], b & 31);
-                on = __shfl_sync(0xFFFFFFFFu, live[i], b & 31);
-            }
-        if (on) acc = fadd(acc, v);
+    for (int i = 0; i < kMaxPerLane; ++i) {
+        if (16 * i >= nb) break;
+        for (int j = 0; j < 16 && 16 * i + j < nb; ++j) {
+            const float v = __shfl_sync(0xFFFFFFFFu, t[i], 2 * j);
+            const bool on = __shfl_sync(0xFFFFFFFFu, live[i], 2 * j);
+            if (on) acc = fadd(acc, v);
+        }
     }
     if (lane == 0) {
         if (a.epilogue == kEpiBias) acc = fadd(acc, a.bias[row]);
