@@ -13,7 +13,8 @@
 // activations in registers (x[b*BS + l + 8k]); a lane may own NBC block columns, and computes them in
 // several rows of each stage (four independent add chains, two for the widest variants).  Rows stream
 // through a shared-memory ring (1-D bulk copies of whole rows, as in gemv_stream.cu); the eight lanes of
-// a column finish a block with three shuffles, and a fold warp adds each row's block terms in block order.
+// a column finish all their block sums together in one transposed butterfly, and a fold warp adds each
+// row's block terms in block order.
 // Rows whose width is not a multiple of the block size (a partial last block has a scalar tail) and the
 // scalar order use the general kernel in gemv.cu (Ternary2) or tb_rowwise_kernel below (bitplanes).
 #include "common.cuh"
@@ -65,9 +66,18 @@ __device__ __forceinline__ bool tn_wait(uint64_t *bar, uint32_t parity, const Tn
     return false;
 }
 
-// One lane's share of one block: the sum of its lane of the eight, then the block's partial (valid in
-// the column's first lane).  LAYOUT 0 = Ternary2 codes, 1 = bitplanes.
-template <int BS, int LAYOUT>
+// The fixed horizontal sum of one block's eight lane partials by three shuffles (the sum is valid in every
+// lane of the column).
+__device__ __forceinline__ float tn_hsum(float a)
+{
+    const float s1 = fadd(a, __shfl_xor_sync(0xFFFFFFFFu, a, 4));     // a_l + a_(l+4)
+    const float s2 = fadd(s1, __shfl_xor_sync(0xFFFFFFFFu, s1, 2));   // (a0+a4) + (a2+a6) | (a1+a5) + (a3+a7)
+    return fadd(s2, __shfl_xor_sync(0xFFFFFFFFu, s2, 1));
+}
+
+// One lane's share of one block: the running sum of its lane of the eight, and with HSUM the block's
+// horizontal sum (otherwise tn_reduce forms it).  LAYOUT 0 = Ternary2 codes, 1 = bitplanes.
+template <int BS, int LAYOUT, bool HSUM>
 __device__ __forceinline__ float tn_block(const uint8_t *blk, const float (&xr)[BS / 8], uint32_t m_lo, uint32_t m_hi)
 {
     const uint32_t *w = reinterpret_cast<const uint32_t *>(blk + 4);
@@ -99,9 +109,7 @@ __device__ __forceinline__ float tn_block(const uint8_t *blk, const float (&xr)[
         }
     }
     (void)m_hi;
-    const float s1 = fadd(a, __shfl_xor_sync(0xFFFFFFFFu, a, 4));     // a_l + a_(l+4)
-    const float s2 = fadd(s1, __shfl_xor_sync(0xFFFFFFFFu, s1, 2));   // (a0+a4) + (a2+a6) | (a1+a5) + (a3+a7)
-    return fadd(s2, __shfl_xor_sync(0xFFFFFFFFu, s2, 1));
+    return HSUM ? tn_hsum(a) : a;
 }
 
 // Whether a variant interleaves its rows' add chains in one loop (tn_blocks) or computes the rows one after
@@ -113,11 +121,21 @@ __host__ __device__ constexpr bool tn_interleave_rows()
     return LAYOUT == 0 && BS == 128 && NBC == 1;
 }
 
-// One lane's share of the same block column in RPL rows: per row, the sum of its lane of the eight, then
-// the block's partial (valid in the column's first lane).  The rows' add chains are interleaved weight by
-// weight so that they overlap; each row's chain is still added in the reference's order.  LAYOUT 0 =
-// Ternary2 codes, 1 = bitplanes.
-template <int BS, int LAYOUT, int RPL>
+// Whether a variant finishes its lane's block sums together in one transposed butterfly (tn_reduce) or
+// each by its own three shuffles (tn_hsum).  Measured at 4096^2 on a B200: the butterfly takes the 64-block
+// kernel from 7.1 to 6.5 us and the 256-block kernel from 6.1 to 5.8 us, but slows the 128-block,
+// one-column kernels (Ternary2 and STB1) from 6.4 to 8.0 us.
+template <int BS, int NBC>
+__host__ __device__ constexpr bool tn_transposed_sum()
+{
+    return !(BS == 128 && NBC == 1);
+}
+
+// One lane's share of the same block column in RPL rows: per row, the running sum of its lane of the
+// eight, and with HSUM the block's horizontal sum.  The rows' add chains are interleaved weight by weight
+// so that they overlap; each row's chain is still added in the reference's order.  LAYOUT 0 = Ternary2
+// codes, 1 = bitplanes.
+template <int BS, int LAYOUT, int RPL, bool HSUM>
 __device__ __forceinline__ void tn_blocks(const uint8_t *const (&blk)[RPL], const float (&xr)[BS / 8], uint32_t m_lo,
                                           uint32_t m_hi, float (&t)[RPL])
 {
@@ -164,13 +182,49 @@ __device__ __forceinline__ void tn_blocks(const uint8_t *const (&blk)[RPL], cons
         }
     }
     (void)m_hi;
-    float s1[RPL], s2[RPL];
+    if constexpr (HSUM) {
+        float s1[RPL], s2[RPL];
 #pragma unroll
-    for (int r = 0; r < RPL; ++r) s1[r] = fadd(a[r], __shfl_xor_sync(0xFFFFFFFFu, a[r], 4));    // a_l + a_(l+4)
+        for (int r = 0; r < RPL; ++r) s1[r] = fadd(a[r], __shfl_xor_sync(0xFFFFFFFFu, a[r], 4));
 #pragma unroll
-    for (int r = 0; r < RPL; ++r) s2[r] = fadd(s1[r], __shfl_xor_sync(0xFFFFFFFFu, s1[r], 2));  // (a0+a4) + (a2+a6) | ...
+        for (int r = 0; r < RPL; ++r) s2[r] = fadd(s1[r], __shfl_xor_sync(0xFFFFFFFFu, s1[r], 2));
 #pragma unroll
-    for (int r = 0; r < RPL; ++r) t[r] = fadd(s2[r], __shfl_xor_sync(0xFFFFFFFFu, s2[r], 1));
+        for (int r = 0; r < RPL; ++r) t[r] = fadd(s2[r], __shfl_xor_sync(0xFFFFFFFFu, s2[r], 1));
+    } else {
+#pragma unroll
+        for (int r = 0; r < RPL; ++r) t[r] = a[r];
+    }
+}
+
+// The fixed horizontal sum ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)) of V lane partials at once, V = 8 or 4,
+// over the eight lanes of a block column (avx = lane & 7), as a transposed butterfly: at each step a lane
+// keeps half of its values and sends the other half to its partner, so every value still meets the same
+// partners in the same tree and only its operand order can differ, which addition ignores.  V = 8: lane
+// avx ends with value avx.  V = 4: lanes 2k and 2k+1 both end with value k.
+template <int V>
+__device__ __forceinline__ float tn_reduce(const float (&v)[V], int avx)
+{
+    static_assert(V == 8 || V == 4, "four or eight values per lane");
+    const bool b2 = avx & 4, b1 = avx & 2, b0 = avx & 1;
+    constexpr int H1 = V / 2, H2 = V / 4;
+    float u[H1];
+#pragma unroll
+    for (int i = 0; i < H1; ++i) {   // a_l + a_(l+4): the low lanes keep values [0, H1), the high lanes the rest
+        const float send = b2 ? v[i] : v[i + H1], keep = b2 ? v[i + H1] : v[i];
+        u[i] = fadd(keep, __shfl_xor_sync(0xFFFFFFFFu, send, 4));
+    }
+    float w[H2];
+#pragma unroll
+    for (int i = 0; i < H2; ++i) {   // (a0+a4) + (a2+a6) on even lanes, (a1+a5) + (a3+a7) on odd lanes
+        const float send = b1 ? u[i] : u[i + H2], keep = b1 ? u[i + H2] : u[i];
+        w[i] = fadd(keep, __shfl_xor_sync(0xFFFFFFFFu, send, 2));
+    }
+    if constexpr (V == 8) {
+        const float send = b0 ? w[0] : w[1], keep = b0 ? w[1] : w[0];
+        return fadd(keep, __shfl_xor_sync(0xFFFFFFFFu, send, 1));
+    } else {
+        return fadd(w[0], __shfl_xor_sync(0xFFFFFFFFu, w[0], 1));
+    }
 }
 
 template <int BS, int NBC, int LAYOUT>
@@ -178,6 +232,7 @@ __global__ void __launch_bounds__((kTnCW + 2) * 32, 2) gemv_ternary_kernel(const
 {
     constexpr int BB = 4 + BS / 4;
     constexpr int RPL = tn_rows_per_lane(NBC);
+    constexpr bool kTransposed = tn_transposed_sum<BS, NBC>();
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -269,7 +324,7 @@ __global__ void __launch_bounds__((kTnCW + 2) * 32, 2) gemv_ternary_kernel(const
                                  (size_t)min(col * NBC + j, a.nblk - 1) * BB;
                     }
                     float tj[RPL];
-                    tn_blocks<BS, LAYOUT, RPL>(blk, xr[j], m_lo, m_hi, tj);
+                    tn_blocks<BS, LAYOUT, RPL, !kTransposed>(blk, xr[j], m_lo, m_hi, tj);
 #pragma unroll
                     for (int r = 0; r < RPL; ++r) t[r][j] = tj[r];
                 }
@@ -280,35 +335,63 @@ __global__ void __launch_bounds__((kTnCW + 2) * 32, 2) gemv_ternary_kernel(const
                     const uint8_t *base = ring + (size_t)s * a.slot + (size_t)min(row, R - 1) * a.row_bytes;
 #pragma unroll
                     for (int j = 0; j < NBC; ++j)
-                        t[r][j] = tn_block<BS, LAYOUT>(base + (size_t)min(col * NBC + j, a.nblk - 1) * BB, xr[j],
-                                                       m_lo, m_hi);
+                        t[r][j] = tn_block<BS, LAYOUT, !kTransposed>(base + (size_t)min(col * NBC + j, a.nblk - 1) * BB,
+                                                                     xr[j], m_lo, m_hi);
                 }
             }
-            // Scales and the blocks' words are read: release the slot, then finish the terms.
-            float scale[RPL][NBC];
+            const int k = fb & 1;   // fold table of this stage
+            if constexpr (kTransposed) {
+                // This lane finishes value vi = (row r, column j) of the V = RPL * NBC block sums of its column.
+                constexpr int V = RPL * NBC;
+                const int vi = V == 8 ? avx : avx >> 1, vr = vi / NBC, vj = vi - vr * NBC;
+                const float scale = *reinterpret_cast<const float *>(
+                    ring + (size_t)s * a.slot + (size_t)min(min(set, a.rl - 1) + vr * a.rl, R - 1) * a.row_bytes +
+                    (size_t)min(col * NBC + vj, a.nblk - 1) * BB);
+                // The blocks' words and the scale are read: release the slot, then finish the terms.
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&h.empty[s]);
+                float v[V];
 #pragma unroll
-            for (int r = 0; r < RPL; ++r) {
-                const int row = min(min(set, a.rl - 1) + r * a.rl, R - 1);
-                const uint8_t *base = ring + (size_t)s * a.slot + (size_t)row * a.row_bytes;
+                for (int r = 0; r < RPL; ++r)
 #pragma unroll
-                for (int j = 0; j < NBC; ++j)
-                    scale[r][j] = *reinterpret_cast<const float *>(base + (size_t)min(col * NBC + j, a.nblk - 1) * BB);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&h.empty[s]);
-            const int k = fb & 1;
-            if (si == 0 && fb >= kTnTables) {
-                if (!tn_wait(&h.dfree[k], (uint32_t)(((fb >> 1) - 1) & 1), h, a.err)) return;
-            }
-            float *dst = dtab + (size_t)k * table_floats + (size_t)si * R * a.pitch;
-            if (active && avx == 0) {
+                    for (int j = 0; j < NBC; ++j) v[r * NBC + j] = t[r][j];
+                const float term = fmul(tn_reduce<V>(v, avx), scale);
+                if (si == 0 && fb >= kTnTables) {
+                    if (!tn_wait(&h.dfree[k], (uint32_t)(((fb >> 1) - 1) & 1), h, a.err)) return;
+                }
+                float *dst = dtab + (size_t)k * table_floats + (size_t)si * R * a.pitch;
+                if (active && (V == 8 || (avx & 1) == 0)) {
+                    const int row = set + vr * a.rl;
+                    if (row < nrows && col * NBC + vj < a.nblk) dst[row * a.pitch + col * NBC + vj] = term;
+                }
+            } else {
+                // Scales and the blocks' words are read: release the slot, then finish the terms.
+                float scale[RPL][NBC];
 #pragma unroll
                 for (int r = 0; r < RPL; ++r) {
-                    const int row = set + r * a.rl;
-                    if (row < nrows) {
+                    const int row = min(min(set, a.rl - 1) + r * a.rl, R - 1);
+                    const uint8_t *base = ring + (size_t)s * a.slot + (size_t)row * a.row_bytes;
 #pragma unroll
-                        for (int j = 0; j < NBC; ++j)
-                            if (col * NBC + j < a.nblk) dst[row * a.pitch + col * NBC + j] = fmul(t[r][j], scale[r][j]);
+                    for (int j = 0; j < NBC; ++j)
+                        scale[r][j] =
+                            *reinterpret_cast<const float *>(base + (size_t)min(col * NBC + j, a.nblk - 1) * BB);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&h.empty[s]);
+                if (si == 0 && fb >= kTnTables) {
+                    if (!tn_wait(&h.dfree[k], (uint32_t)(((fb >> 1) - 1) & 1), h, a.err)) return;
+                }
+                float *dst = dtab + (size_t)k * table_floats + (size_t)si * R * a.pitch;
+                if (active && avx == 0) {
+#pragma unroll
+                    for (int r = 0; r < RPL; ++r) {
+                        const int row = set + r * a.rl;
+                        if (row < nrows) {
+#pragma unroll
+                            for (int j = 0; j < NBC; ++j)
+                                if (col * NBC + j < a.nblk)
+                                    dst[row * a.pitch + col * NBC + j] = fmul(t[r][j], scale[r][j]);
+                        }
                     }
                 }
             }
