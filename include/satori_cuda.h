@@ -89,6 +89,8 @@ SATORI_API void *satori_stream(satori_ctx *ctx);
 /* Routes the context's device work to a caller-owned cudaStream_t (NULL restores the context's own
  * stream), e.g. to capture device-pointer calls into the caller's CUDA graph. */
 SATORI_API int satori_set_stream(satori_ctx *ctx, void *stream);
+/* Waits for the work queued on the context's current stream; reports a device error a kernel recorded
+ * (SATORI_ERR_TIMEOUT for an expired bounded wait) like the synchronous calls do. */
 SATORI_API int satori_synchronize(satori_ctx *ctx);
 
 /* ------------------------------------------------------------------ matrices */
@@ -120,6 +122,7 @@ SATORI_API int satori_matrix_execute_device(satori_matrix *m, const float *dx, f
  * bit-exact; Q4_0 rows are rejected with SATORI_ERR_NOT_SUPPORTED as in the reference.  For
  * Ternary2 it decodes one row like Ternary2Matrix.Dequantize (Ternary2Matrix.cs:103-120). */
 SATORI_API int satori_matrix_read_row(satori_matrix *m, int row, float *out);
+/* The matrix's shape, satori_format and payload length (IQuantizedMatrix.Rows / Columns). */
 SATORI_API int satori_matrix_info(const satori_matrix *m, int *rows, int *cols, int *format, size_t *bytes);
 /* Device address of the resident payload (read-only), e.g. for a caller-managed graph. */
 SATORI_API const uint8_t *satori_matrix_device_payload(const satori_matrix *m);
@@ -204,8 +207,8 @@ SATORI_API int satori_session_create(satori_ctx *ctx, const satori_model_desc *d
  * by query heads, each rank caching only the KV heads its heads read; the context, the residual
  * after attn_output / ffn_down, the SwiGLU activations and the logits are all-gathered inside the
  * step's CUDA graph -- by default with peer stores over NVLink into IPC-mapped buffers, carried by the
- * producing MatVec launches where they can (SATORI_EXCHANGE=nccl selects NCCL all-gathers).  hidden, ffn and vocab must be multiples of `world`
- * (SATORI_ERR_NOT_SUPPORTED otherwise).  Every rank passes the full tensor table and uploads only
+ * producing MatVec launches where they can (SATORI_EXCHANGE=nccl selects NCCL all-gathers).  hidden,
+ * ffn and vocab must be multiples of `world` (SATORI_ERR_NOT_SUPPORTED otherwise).  Every rank passes the full tensor table and uploads only
  * its rows.  `nccl_unique_id` is the 128-byte id from satori_nccl_unique_id on rank 0.  world = 1 is
  * satori_session_create. */
 SATORI_API int satori_session_create_sharded(satori_ctx *ctx, const satori_model_desc *desc, int context, int rank,
@@ -229,6 +232,7 @@ SATORI_API int satori_matrix_create_sharded(satori_ctx *ctx, const uint8_t *payl
 SATORI_API int satori_matrix_sharded_execute_device(satori_matrix_sharded *m, const float *dx, float *dy, int order);
 /* Host vectors, synchronous; y committed only on success. */
 SATORI_API int satori_matrix_sharded_execute(satori_matrix_sharded *m, const float *x, float *y, int order);
+/* The rows [row_begin, row_end) this rank holds and computes. */
 SATORI_API int satori_matrix_sharded_info(const satori_matrix_sharded *m, int *row_begin, int *row_end);
 SATORI_API int satori_matrix_sharded_destroy(satori_matrix_sharded *m);
 /* DenseSession.Append (DenseSession.cs:111-131) + GreedyTokenSelector.Select
@@ -249,6 +253,7 @@ SATORI_API int satori_session_forward_tensor(satori_session *s, const int *token
 /* Greedy generation: appends `first`, then feeds back the argmax `count - 1` more times; writes the
  * `count` greedy tokens (TextGenerator.GenerateFromTokens' decode loop, TextGenerator.cs:62-99). */
 SATORI_API int satori_session_generate(satori_session *s, int first, int count, int *tokens_out);
+/* DenseSession.Position (DenseSession.cs:96): the number of cached positions. */
 SATORI_API int satori_session_position(const satori_session *s, int *position);
 SATORI_API int satori_session_reset(satori_session *s);    /* DenseSession.Reset (:189) */
 /* No counterpart in the reference (its DenseSession only resets to position 0): discards the
