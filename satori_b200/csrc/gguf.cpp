@@ -352,7 +352,8 @@ void satori_gguf::parse()
 
 namespace {
 
-int map_file(const char *path, int *fd_out, const uint8_t **map_out, int64_t *len_out)
+// Maps `path` read-only.  A file longer than `limit` bytes is refused before it is mapped (GgufFile.cs:21).
+int map_file(const char *path, int64_t limit, int *fd_out, const uint8_t **map_out, int64_t *len_out)
 {
     const int fd = open(path, O_RDONLY | O_CLOEXEC);
     if (fd < 0) return set_error(SATORI_ERR_ARGUMENT, "cannot open %s: %s", path, strerror(errno));
@@ -360,6 +361,10 @@ int map_file(const char *path, int *fd_out, const uint8_t **map_out, int64_t *le
     if (fstat(fd, &st) != 0) {
         close(fd);
         return set_error(SATORI_ERR_ARGUMENT, "cannot stat %s", path);
+    }
+    if ((int64_t)st.st_size > limit) {
+        close(fd);
+        return set_error(SATORI_ERR_NOT_SUPPORTED, "File limit: 1 TiB.");
     }
     *fd_out = fd;
     *len_out = (int64_t)st.st_size;
@@ -466,10 +471,9 @@ extern "C" int satori_gguf_open(const char *path, satori_gguf **out)
 {
     if (!path || !out) return set_error(SATORI_ERR_ARGUMENT, "null argument");
     std::unique_ptr<satori_gguf> g(new satori_gguf());
-    int rc = map_file(path, &g->fd, &g->map, &g->length);
+    int rc = map_file(path, kFileLimit, &g->fd, &g->map, &g->length);
     if (rc) return rc;
     if (g->length == 0) return set_error(SATORI_ERR_INVALID_DATA, "GGUF at byte 0: empty file.");
-    if (g->length > kFileLimit) return set_error(SATORI_ERR_NOT_SUPPORTED, "File limit: 1 TiB.");
     try {
         g->parse();
     } catch (const GgufError &e) {
@@ -722,7 +726,7 @@ extern "C" int satori_stq2_open(satori_ctx *ctx, const char *path, satori_matrix
     int fd = -1;
     const uint8_t *map = nullptr;
     int64_t len = 0;
-    int rc = map_file(path, &fd, &map, &len);
+    int rc = map_file(path, INT64_MAX, &fd, &map, &len);
     if (rc) return rc;
     auto done = [&](int status) {
         if (map) munmap(const_cast<uint8_t *>(map), (size_t)len);

@@ -97,13 +97,20 @@ class GgufFile:
             return raw[0] != 0
         return struct.unpack(_FMT[typ.value], raw)[0]
 
-    def read_tensor(self, name: str) -> np.ndarray:
-        """GgufFile.ReadTensor over the whole payload: a copy of the tensor's bytes."""
+    def read_tensor(self, name: str, offset: int = 0, length: int | None = None) -> np.ndarray:
+        """GgufFile.ReadTensor (src/Satori.Formats.Gguf/GgufFile.cs:42-48): a copy of the window
+        [offset, offset + length) of the tensor's payload, the rest of the payload when ``length`` is None.
+        A window outside the payload raises ArgumentError (ArgumentOutOfRangeException) before the
+        mapping is touched; a closed file raises DisposedError."""
         t = self.tensors[name]
+        if length is None:
+            length = t.byte_length - offset
+        if offset < 0 or length < 0 or offset > t.byte_length or length > t.byte_length - offset:
+            raise _lib.ArgumentError(_lib.ERR_ARGUMENT, "Window exceeds tensor payload.")
         idx = C.c_int()
         check(_lib.lib().satori_gguf_find_tensor(self.handle, name.encode(), C.byref(idx)), "find_tensor")
         ptr = _lib.lib().satori_gguf_tensor_data(self.handle, idx.value)
-        return np.frombuffer(C.string_at(ptr, t.byte_length), dtype=np.uint8).copy()
+        return np.frombuffer(C.string_at(ptr + offset, length), dtype=np.uint8).copy()
 
     def model_desc(self) -> dict:
         """DenseTransformerAdapter.Validate: the model shape the file describes."""

@@ -49,6 +49,13 @@ def test_golden_catalogue(sat, oracle_lib, tmp_path, name, type_id, length, offs
         else:
             decoded = payload.view(np.float32 if type_id == 0 else np.float16).astype(np.float32)
         assert decoded.tolist() == f["decoded_weights"]
+        # scoped bounds: a window past the payload is refused, an empty one at its end is empty
+        with pytest.raises(sat.ArgumentError):
+            g.read_tensor("weights", length, 1)
+        assert g.read_tensor("weights", length, 0).size == 0
+        assert g.read_tensor("weights", 1, 2).tolist() == payload[1:3].tolist()
+    with pytest.raises(sat.DisposedError):
+        g.read_tensor("weights", 0, 1)
 
 
 def test_every_truncation_rejects(sat, tmp_path):
@@ -81,6 +88,44 @@ def test_repeated_reads_are_stable(sat, tmp_path):
             assert g.read_scalar("general.architecture") == "llama"
             assert g.read_scalar("general.quantization_version") == 2
             assert g.tensors["weights"].type == 8
+
+
+def _sparse(tmp_path, name, length, head=b"", tail_at=None, tail=b""):
+    """A file of `length` bytes written only where given (MappedFileFixture with a sparse body)."""
+    p = tmp_path / name
+    with open(p, "wb") as f:
+        f.write(head)
+        if tail_at is not None:
+            f.seek(tail_at)
+            f.write(tail)
+        f.truncate(length)
+    return str(p)
+
+
+def test_oversized_sparse_file_rejects_before_mapping(sat, tmp_path):
+    """GgufStructureTests.OversizedSparseFileRejectsBeforeMapping (GgufStructureTests.cs:57-63)."""
+    try:
+        path = _sparse(tmp_path, "huge.gguf", (1 << 40) + 1)
+    except OSError as e:   # a file system without sparse files of that size
+        pytest.skip(f"cannot create a sparse 1 TiB file here: {e}")
+    with pytest.raises(sat.NotSupportedError, match="File limit"):
+        sat.GgufFile(path)
+
+
+def test_sparse_tensor_beyond_two_gib(sat, tmp_path):
+    """GgufStructureTests.SparseTensorBeyondTwoGiBUsesInt64Windows (GgufStructureTests.cs:84-99): offsets
+    past 2^31 are 64-bit, and a window reaching past a tensor is refused."""
+    first = 1 << 31
+    head = G.prefix(32, tensors=[("large", [first // 4], G.T_F32, 0), ("tail", [1], G.T_F32, first)])
+    try:
+        path = _sparse(tmp_path, "big.gguf", len(head) + first + 32, head, len(head) + first, bytes([1, 2, 3, 4]))
+    except OSError as e:
+        pytest.skip(f"cannot create a sparse 2 GiB file here: {e}")
+    with sat.GgufFile(path) as g:
+        assert g.tensors["tail"].offset == len(head) + first
+        assert g.read_tensor("tail", 0, 4).tolist() == [1, 2, 3, 4]
+        with pytest.raises(sat.ArgumentError):
+            g.read_tensor("large", first - 1, 2)
 
 
 def test_closed_file_refuses_access(sat, tmp_path):
