@@ -248,3 +248,89 @@ def test_model_description_from_metadata(sat, tmp_path):
     with sat.GgufFile(_file(tmp_path, G.model_gguf(spec, broken), "broken.gguf")) as g:
         with pytest.raises(sat.NotSupportedError):
             g.model_desc()
+
+
+def _qwen_container(tmp_path, name, arch="qwen2", embedding=64, heads=2, heads_kv=1, ffn=64, vocab=10, layers=2,
+                    key_length=None, drop_meta=(), shapes=None):
+    """A qwen-style container with Q8_0 matrices (zero payload) and F32 norms in canonical order, for the
+    model-description rules (ModelDescriptorTests' Qwen2 helper, written as a GGUF file)."""
+    head_dim = key_length or max(1, embedding // heads)
+    q, kv = heads * head_dim, heads_kv * head_dim
+    meta = [(f"{arch}.block_count", G.U32, layers), (f"{arch}.embedding_length", G.U32, embedding),
+            (f"{arch}.feed_forward_length", G.U32, ffn), (f"{arch}.attention.head_count", G.U32, heads),
+            (f"{arch}.attention.head_count_kv", G.U32, heads_kv),
+            (f"{arch}.attention.layer_norm_rms_epsilon", G.F32, 1e-6), (f"{arch}.rope.freq_base", G.F32, 1e6),
+            ("general.quantization_version", G.U32, 2)]
+    if key_length is not None:
+        meta.append((f"{arch}.attention.key_length", G.U32, key_length))
+    meta = [m for m in meta if m[0].split(".", 1)[1] not in drop_meta]
+    want = [("token_embd.weight", [embedding, vocab]), ("output_norm.weight", [embedding])]
+    for l in range(layers):
+        p = f"blk.{l}."
+        want += [(p + "attn_norm.weight", [embedding]), (p + "attn_q.weight", [embedding, q]),
+                 (p + "attn_k.weight", [embedding, kv]), (p + "attn_v.weight", [embedding, kv]),
+                 (p + "attn_output.weight", [q, embedding]), (p + "ffn_norm.weight", [embedding]),
+                 (p + "ffn_gate.weight", [embedding, ffn]), (p + "ffn_up.weight", [embedding, ffn]),
+                 (p + "ffn_down.weight", [ffn, embedding])]
+    want = [(n, (shapes or {}).get(n, d)) for n, d in want]
+    tensors, off = [], 0
+    for n, dims in want:
+        t = G.T_Q8_0 if len(dims) == 2 else G.T_F32
+        nbytes = dims[0] // 32 * 34 * dims[1] if t == G.T_Q8_0 else 4 * dims[0]
+        tensors.append((n, dims, t, off))
+        off = (off + nbytes + 31) // 32 * 32
+    head = G.prefix(32, b"".join(G.entry(*m) for m in meta), len(meta), tensors, arch=arch)
+    return _file(tmp_path, G.file_with(head, len(head) + off), name)
+
+
+def test_dense_adapter_derives_shape(sat, tmp_path):
+    """ModelDescriptorTests.DenseAdapterDerivesShapeAndReportsNoGaps (ModelDescriptorTests.cs:11-23): the head
+    length is embedding / heads when no key_length is declared; the vocabulary comes from token_embd."""
+    with sat.GgufFile(_qwen_container(tmp_path, "a.gguf")) as g:
+        d = g.model_desc()
+    assert (d["layers"], d["hidden"], d["head_dim"], d["kv_heads"], d["vocab"]) == (2, 64, 32, 1, 10)
+    assert d["tied_embeddings"]          # no output.weight: the embedding is the output projection
+    assert d["tensors"] == 2 + 2 * 9
+
+
+def test_explicit_key_length_overrides_hidden_over_heads(sat, tmp_path):
+    """ModelDescriptorTests.ExplicitKeyLengthOverridesHiddenOverHeads (ModelDescriptorTests.cs:25-35)."""
+    with sat.GgufFile(_qwen_container(tmp_path, "k.gguf", layers=1, key_length=48)) as g:
+        assert g.model_desc()["head_dim"] == 48
+
+
+def test_incompatible_shape_is_reported(sat, tmp_path):
+    """ModelDescriptorTests.IncompatibleShapeIsReported (ModelDescriptorTests.cs:37-48): the wrong tensor is named."""
+    path = _qwen_container(tmp_path, "s.gguf", layers=1, shapes={"blk.0.attn_q.weight": [64, 999]})
+    with sat.GgufFile(path) as g:
+        with pytest.raises(sat.NotSupportedError, match="blk.0.attn_q.weight"):
+            g.model_desc()
+
+
+def test_indivisible_embedding_without_key_length_is_reported(sat, tmp_path):
+    """ModelDescriptorTests.UndeclaredHeadLengthWithIndivisibleEmbeddingIsReported (ModelDescriptorTests.cs:50-56)."""
+    path = _qwen_container(tmp_path, "i.gguf", embedding=96, heads=5, layers=1,
+                           shapes={"blk.0.attn_output.weight": [96, 96]})   # any whole-block width parses
+    with sat.GgufFile(path) as g:
+        with pytest.raises(sat.NotSupportedError, match="attention.key_length"):
+            g.model_desc()
+
+
+def test_missing_required_metadata_is_reported(sat, tmp_path):
+    """ModelDescriptorTests.MissingRequiredMetadataIsReported (ModelDescriptorTests.cs:58-70)."""
+    drop = ("embedding_length", "feed_forward_length", "attention.head_count", "attention.head_count_kv")
+    with sat.GgufFile(_qwen_container(tmp_path, "m.gguf", layers=1, drop_meta=drop)) as g:
+        with pytest.raises(sat.NotSupportedError, match="embedding_length"):
+            g.model_desc()
+
+
+@pytest.mark.parametrize("arch,supported", [("qwen3", True), ("mysterymoe", False)])
+def test_architecture_adapter(sat, tmp_path, arch, supported):
+    """ModelDescriptorTests.UnknownArchitectureHasNoAdapter (ModelDescriptorTests.cs:72-77): qwen2 and qwen3
+    resolve, any other architecture has no dense adapter."""
+    with sat.GgufFile(_qwen_container(tmp_path, arch + ".gguf", arch=arch, layers=1)) as g:
+        if supported:
+            assert g.model_desc()["layers"] == 1
+        else:
+            with pytest.raises(sat.NotSupportedError):
+                g.model_desc()
