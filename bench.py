@@ -18,7 +18,8 @@ token (identical) with the CPU oracle's DenseSession restatement; the line carri
 At N = 1 the line also carries `kernels` (each hot kernel alone, >= 5 repeats of >= 0.5 s regions,
 min / median / spread): configs[1] MatVec, configs[2] attention at T = 512 / 4096 / 32768 and
 configs[0] Ternary2 4096^2 at block 64 / 128 / 256; and `cpu_baseline`: the oracle's decode step on
-the host cores at the same context, all threads and one thread.
+the host cores at the same context, all threads and one thread, with `cpu_baseline.kernels` holding
+the oracle's configs[0] / [1] / [2] kernels on one thread and on all threads.
 
 --impl reference times the reference's CPU path (the oracle's C restatement of DenseSession.Append,
 all host threads; the C# reference cannot run in this image) on the same metric and config.
@@ -654,6 +655,57 @@ def cpu_baseline_decode(spec, host, context):
             "cpu_model": _cpu_model()}
 
 
+def _cpu_rate(call, nbytes, min_s):
+    """GB/s of one host call repeated for at least `min_s` seconds, after one untimed call."""
+    call()
+    n, t0 = 0, time.perf_counter()
+    while n < 1 or time.perf_counter() - t0 < min_s:
+        call()
+        n += 1
+    dt = time.perf_counter() - t0
+    return nbytes / (dt / n) / GB, n, dt
+
+
+def cpu_kernel_baselines(min_s=0.5):
+    """The oracle's restatements of the kernel-level configs on the host cores, on one thread and on all
+    threads, beside the GPU kernel records: configs[0] Ternary2Avx2Kernel at 4096^2 (bs 64 / 128 / 256),
+    configs[1] ExecuteBatchFloat over Q8_0 4096^2 + Q4_0 11008x4096, configs[2] GroupedAttention (FP64) at
+    28/4 heads x 128, T = 4096.  Seeded host inputs with the GPU records' shapes and distributions."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(21)
+    all_threads = os.cpu_count() or 1
+    out = {}
+
+    def record(name, call, nbytes, workload):
+        v1, n1, d1 = _cpu_rate(lambda: call(1), nbytes, min_s)
+        va, na, da = _cpu_rate(lambda: call(all_threads), nbytes, min_s)
+        out[name] = {"value_1_thread": round(v1, 3), "value_all_threads": round(va, 3), "unit": "GB/s",
+                     "cores": all_threads, "algorithmic_bytes_per_unit": int(nbytes), "workload": workload,
+                     "sample": f"{n1} calls in {d1:.2f}s on 1 thread, {na} calls in {da:.2f}s on {all_threads}"}
+
+    n = 4096
+    w = rng.standard_normal(n * n).astype(np.float32)
+    x = rng.standard_normal(n).astype(np.float32)
+    for bs in (64, 128, 256):
+        p = O.t2_quantize(w, n, n, bs)
+        record(f"ternary2_4096x4096_bs{bs}", lambda t, p=p, bs=bs: O.t2_matvec(p, n, n, bs, x, "avx2", threads=t),
+               p.size, f"configs[0] bs{bs}, Ternary2Avx2Kernel order")
+    del w
+    p8 = O.q_quantize((0.02 * rng.standard_normal(n * n)).astype(np.float32), n, n, 0)
+    p4 = O.q_quantize((0.02 * rng.standard_normal(11008 * n)).astype(np.float32), 11008, n, 1)
+    record("matvec_q8_0_4096x4096+q4_0_11008x4096",
+           lambda t: (O.q_matvec(p8, n, n, 0, x, "batch", threads=t), O.q_matvec(p4, 11008, n, 1, x, "batch", threads=t)),
+           p8.size + p4.size, "configs[1], ExecuteBatchFloat order")
+    del p8, p4
+    T, qh, kvh, hd = 4096, 28, 4, 128
+    q = rng.standard_normal(qh * hd).astype(np.float32)
+    keys = rng.standard_normal(T * kvh * hd).astype(np.float32)
+    values = rng.standard_normal(T * kvh * hd).astype(np.float32)
+    record(f"attention_T{T}", lambda t: O.grouped_attention(q, keys, values, qh, kvh, hd, T, threads=t),
+           2 * T * kvh * hd * 4, "configs[2] 28/4 x 128, GroupedAttention (FP64)")
+    return out
+
+
 def _embedding_table_bytes(spec, world):
     """Bytes of token_embd.weight inside a session's weight bytes that a step does not stream (a step
     reads one row): the whole table, unless it is also the single-GPU output matrix."""
@@ -746,6 +798,10 @@ def bench_decode(args, rank, world, local, spec, with_kernels: bool):
         res["kernels"] = kernels_record(ctx, min_region_s=args.region, repeats=args.repeats)
     if rank == 0 and world == 1 and host is not None and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline_decode(spec, host, P)
+        try:   # the kernel-level CPU figures are context for the kernel records; never fatal to the line
+            res["cpu_baseline"]["kernels"] = cpu_kernel_baselines()
+        except Exception as e:
+            res["cpu_baseline"]["kernels"] = {"error": f"{type(e).__name__}: {e}"[:300]}
     return res
 
 
