@@ -77,7 +77,11 @@ typedef struct satori_session satori_session;
 
 /* ------------------------------------------------------------------ context */
 /* Opens device `device` (one context per caller; replaces VulkanContext.TryCreate,
- * src/Satori.Backends.Vulkan/VulkanContext.cs:57). */
+ * src/Satori.Backends.Vulkan/VulkanContext.cs:57).  A process may hold contexts on several devices and
+ * call from any thread: the entry points that take host buffers, allocate or run a session step make
+ * the handle's device current for the call and then restore the caller's.  The device-pointer entry
+ * points (..._device, satori_grouped_attention_noalloc) run on the calling thread's current device,
+ * which must be the one that holds the pointers (and the context's device). */
 SATORI_API int satori_init(int device, satori_ctx **out);
 SATORI_API int satori_destroy(satori_ctx *ctx);
 /* Copies the calling thread's last error message (NUL-terminated, truncated to n). */

@@ -402,6 +402,8 @@ extern "C" int satori_set_stream(satori_ctx *ctx, void *stream)
 extern "C" int satori_synchronize(satori_ctx *ctx)
 {
     if (!ctx) return set_error(SATORI_ERR_ARGUMENT, "ctx is null");
+    DeviceScope scope(ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     return check_dev_error(ctx);
 }
 
@@ -410,6 +412,8 @@ static int matrix_create(satori_ctx *ctx, const uint8_t *payload, bool dev, size
                          int format, satori_matrix **out)
 {
     if (!ctx || !out) return set_error(SATORI_ERR_ARGUMENT, "ctx/out is null");
+    DeviceScope scope(ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     uint8_t *d = nullptr;
     int rc = upload_payload(ctx, payload, dev, bytes, rows, cols, format, &d);
     if (rc) return rc;
@@ -465,6 +469,8 @@ static int matrix_execute_host(satori_matrix *m, const float *x, float *y, int p
     const char *yb = (const char *)y, *ye = yb + (size_t)positions * m->rows * 4;
     if (xb < ye && yb < xe) return set_error(SATORI_ERR_ARGUMENT, "output must not overlap input");
     satori_ctx *ctx = m->ctx;
+    DeviceScope scope(ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     int rc = ensure_work(m, positions);
     if (rc) return rc;
     memcpy(m->h_x, x, (size_t)positions * m->cols * 4);
@@ -529,6 +535,8 @@ extern "C" int satori_matrix_read_row(satori_matrix *m, int row, float *out)
     if (!m) return set_error(SATORI_ERR_DISPOSED, "matrix is disposed");
     if (m->format == SATORI_Q4_0) return set_error(SATORI_ERR_NOT_SUPPORTED, "Q4_0 embedding rows are not supported");
     if (row < 0 || row >= m->rows || !out) return set_error(SATORI_ERR_ARGUMENT, "row %d out of range", row);
+    DeviceScope scope(m->ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     int rc = ensure_work(m, 1);
     if (rc) return rc;
     satori_ctx *ctx = m->ctx;
@@ -575,6 +583,8 @@ extern "C" int satori_ternary2_quantize(satori_ctx *ctx, const float *weights, i
         return set_error(SATORI_ERR_ARGUMENT, "Supported block sizes: 64, 128, 256.");
     int rc = validate_shape(rows, cols, block_size);
     if (rc) return rc;
+    DeviceScope scope(ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     const size_t n = (size_t)rows * cols, bytes = payload_bytes(rows, cols, block_size);
     float *dw = nullptr;
     uint8_t *dp = nullptr;
@@ -678,6 +688,8 @@ extern "C" int satori_grouped_attention(satori_ctx *ctx, const float *q, const f
     if (!ctx || !q || !keys || !values || !out) return set_error(SATORI_ERR_ARGUMENT, "null argument");
     int rc = attention_args_ok(q_heads, kv_heads, head_dim, tokens);
     if (rc) return rc;
+    DeviceScope scope(ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     const size_t nq = (size_t)q_heads * head_dim, nkv = (size_t)tokens * kv_heads * head_dim;
     float *dq = nullptr, *dk = nullptr, *dv = nullptr, *dout = nullptr;
     cudaError_t e = cudaMalloc(&dq, nq * 4);
@@ -715,6 +727,8 @@ extern "C" int satori_rope_half(satori_ctx *ctx, float *vector, int n, int head_
     if (head_dim <= 0 || n % head_dim != 0 || position < 0) return set_error(SATORI_ERR_ARGUMENT, "headDimension");
     if (!(base > 0) || isinf(base)) return set_error(SATORI_ERR_ARGUMENT, "frequencyBase");
     if (rotary <= 0 || rotary > head_dim || rotary % 2 != 0) return set_error(SATORI_ERR_ARGUMENT, "rotaryDimensions");
+    DeviceScope scope(ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     float *d = nullptr;
     std::vector<float> host(n);
     cudaError_t e = cudaMalloc(&d, (size_t)n * 4 + 4);
@@ -745,6 +759,8 @@ extern "C" int satori_attn_create(satori_ctx *ctx, int layers, int context, int 
     if (layers <= 0 || context <= 0) return set_error(SATORI_ERR_ARGUMENT, "layers/context must be positive");
     int rc = attention_args_ok(q_heads, kv_heads, head_dim, 1);
     if (rc) return rc;
+    DeviceScope scope(ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     satori_attn *a = new satori_attn();
     a->ctx = ctx;
     a->layers = layers;
@@ -783,6 +799,8 @@ extern "C" int satori_attn_append(satori_attn *a, int layer, int position, const
     if (position >= a->context)
         return set_error(SATORI_ERR_CONTEXT_FULL, "Context limit %d reached; reset or enlarge the session.", a->context);
     satori_ctx *ctx = a->ctx;
+    DeviceScope scope(ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     const size_t kvw = (size_t)a->kv_heads * a->head_dim, qw = (size_t)a->q_heads * a->head_dim;
     float *kc = a->d_k + (size_t)layer * a->context * kvw, *vc = a->d_v + (size_t)layer * a->context * kvw;
     cudaError_t e = clear_dev_error(ctx);

@@ -42,6 +42,28 @@ namespace satori {
 
 int set_error(int status, const char *fmt, ...);
 int cuda_fail(cudaError_t e, const char *what);
+
+// Makes a handle's device current for one entry point and gives the caller's device back at the end:
+// a process may hold contexts on several GPUs and call the library from any thread, and allocations,
+// copies and launches must land on the handle's device.  When that device is already current (one GPU
+// per process) nothing changes.  The device-pointer entry points do not take one: they work on the
+// caller's current device, which a caller capturing them into a CUDA graph has already chosen.
+struct DeviceScope {
+    int prev = -1, dev;
+    cudaError_t status = cudaSuccess;
+    explicit DeviceScope(int device) : dev(device)
+    {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) status = cudaSetDevice(dev);
+    }
+    ~DeviceScope()
+    {
+        if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+    }
+    DeviceScope(const DeviceScope &) = delete;
+    DeviceScope &operator=(const DeviceScope &) = delete;
+};
+
 // Clears the context's device error word on its stream.
 cudaError_t clear_dev_error(satori_ctx *ctx);
 // Reads the device error word (synchronises the stream) and maps it to a status.

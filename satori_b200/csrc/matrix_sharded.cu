@@ -139,6 +139,8 @@ extern "C" int satori_matrix_sharded_execute(satori_matrix_sharded *m, const flo
     if (!m) return set_error(SATORI_ERR_DISPOSED, "matrix is disposed");
     if (!x || !y) return set_error(SATORI_ERR_ARGUMENT, "vector is null");
     satori_ctx *ctx = m->ctx;
+    DeviceScope scope(ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     cudaError_t e = cudaSuccess;
     if (!m->d_x) {
         e = cudaMalloc(&m->d_x, (size_t)m->cols * 4);

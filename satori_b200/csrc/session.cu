@@ -539,6 +539,8 @@ int session_dalloc_bytes(satori_session *s, void **p, size_t bytes)
 extern "C" int satori_session_create(satori_ctx *ctx, const satori_model_desc *d, int context, satori_session **out)
 {
     if (!ctx || !out) return set_error(SATORI_ERR_ARGUMENT, "null argument");
+    DeviceScope scope(ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     TRY(check_desc(d, context));
     return session_build(session_new(ctx, d, context), d, out);
 }
@@ -563,6 +565,8 @@ static int step_status(satori_session *s)
 static int run_steps(satori_session *s, const int *feed, int count, float *logits, int *argmax)
 {
     if (!s) return set_error(SATORI_ERR_DISPOSED, "session is disposed");
+    DeviceScope scope(s->ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     if (s->failed) return peer_lost(s);
     if (count <= 0) return set_error(SATORI_ERR_ARGUMENT, "count must be positive");
     for (int i = 0; i < count; ++i)
@@ -609,6 +613,8 @@ extern "C" int satori_session_append_tokens(satori_session *s, const int *tokens
 extern "C" int satori_session_generate(satori_session *s, int first, int count, int *tokens_out)
 {
     if (!s) return set_error(SATORI_ERR_DISPOSED, "session is disposed");
+    DeviceScope scope(s->ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     if (s->failed) return peer_lost(s);
     if (!tokens_out) return set_error(SATORI_ERR_ARGUMENT, "tokens_out is null");
     if (first < 0 || first >= s->vocab) return set_error(SATORI_ERR_ARGUMENT, "Token %d is outside the vocabulary.", first);
@@ -651,6 +657,8 @@ extern "C" int satori_session_position(const satori_session *s, int *position)
 extern "C" int satori_session_reset(satori_session *s)
 {
     if (!s) return set_error(SATORI_ERR_DISPOSED, "session is disposed");
+    DeviceScope scope(s->ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     s->position = 0;
     cudaError_t e = cudaMemsetAsync(s->d_pos, 0, sizeof(int), s->ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s->ctx->stream);
@@ -663,6 +671,8 @@ extern "C" int satori_session_rewind(satori_session *s, int position)
     if (position < 0 || position > s->position)
         return set_error(SATORI_ERR_ARGUMENT, "position %d is outside the committed range [0, %d]", position,
                          s->position);
+    DeviceScope scope(s->ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     // The cache rows below `position` are untouched; the next step overwrites row `position`.
     s->position = position;
     s->h_ints[6] = position;
@@ -687,6 +697,8 @@ extern "C" int satori_session_stage(const satori_session *s, int which, float *o
     const float *src = which == 0 ? s->d_hidden : which == 1 ? s->d_final : which == 2 ? s->d_logits : nullptr;
     const size_t len = which == 2 ? (size_t)s->vocab : (size_t)s->hidden;
     if (!src || !out || n != len) return set_error(SATORI_ERR_ARGUMENT, "bad stage %d / length %zu", which, n);
+    DeviceScope scope(s->ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     cudaError_t e = cudaMemcpyAsync(out, src, len * 4, cudaMemcpyDeviceToHost, s->ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s->ctx->stream);
     return e == cudaSuccess ? SATORI_OK : cuda_fail(e, "stage");

@@ -191,6 +191,8 @@ extern "C" int satori_session_forward_tensor(satori_session *s, const int *token
                                              int *argmax)
 {
     if (!s) return set_error(SATORI_ERR_DISPOSED, "session is disposed");
+    DeviceScope scope(s->ctx->device);
+    if (scope.status != cudaSuccess) return cuda_fail(scope.status, "cudaSetDevice");
     if (!tokens) return set_error(SATORI_ERR_ARGUMENT, "tokens is null");
     if (count <= 0) return set_error(SATORI_ERR_ARGUMENT, "count must be positive");
     for (int i = 0; i < count; ++i)
