@@ -20,6 +20,10 @@ here once, as data, together with where each came from:
   tools/attention_reference.py:4-6, restated in tests/golden_util.py.
 * The Ternary2 encoding KAT (Ternary2Tests.cs:9-22) and the STQ2 header KAT
   (MappedTernary2Tests.cs:40-46) are byte strings stated in those tests; they are copied too.
+* ``docs/scouting/inventories/qwen2.5-coder-{1.5b-q8_0,7b-q4_0}.json`` -- the GGUF catalogues of two
+  real models (scalar metadata, every tensor's name / type / dimensions / offset / length) and the plan
+  of ``docs/benchmarks/qwen-2026-10-13/qwen2.5-coder-1.5b-q8_0-ctx2048.json`` (shape, weight and KV
+  state bytes), for the model-shape and native-loader tests.
 """
 from __future__ import annotations
 
@@ -31,7 +35,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "reference_fixtures.json")
 
 
-def main(ref: str) -> None:
+def main(ref: str, out_path: str = OUT) -> None:
     gguf_dir = os.path.join(ref, "fixtures", "gguf", "v1")
     manifest = json.load(open(os.path.join(gguf_dir, "manifest.json")))
     gguf = {}
@@ -75,8 +79,30 @@ def main(ref: str) -> None:
                     "attention_head_dim": 48, "attention_tokens": 7,
                     "stated_in": "tests/Satori.Numerics.Tests/TransformerOpsTests.cs:19-24"}
 
+    # Catalogues of two real models as the reference's GGUF inventory recorded them (scalar metadata and
+    # every tensor's name, type, dimensions, relative offset and length; the arrays' values are not
+    # recorded there), and the plan the reference's benchmark reported for the 1.5B model at context 2048.
+    inventories = {}
+    for name in ("qwen2.5-coder-1.5b-q8_0", "qwen2.5-coder-7b-q4_0"):
+        inv = json.load(open(os.path.join(ref, "docs", "scouting", "inventories", name + ".json")))
+        meta = [[m["Key"], m["TypeName"], m["Value"]] for m in inv["Metadata"]
+                if m["TypeName"] != "Array" and not m["Key"].startswith("tokenizer.chat")]
+        inventories[name] = {
+            "source": f"docs/scouting/inventories/{name}.json",
+            "tensor_count": inv["TensorCount"], "alignment": inv["Alignment"],
+            "total_tensor_bytes": inv["TotalTensorBytes"], "metadata": meta,
+            "tensors": [[t["Name"], t["TypeId"], t["Dimensions"], t["Offset"], t["ByteLength"]] for t in inv["Tensors"]],
+        }
+    bench = json.load(open(os.path.join(ref, "docs", "benchmarks", "qwen-2026-10-13",
+                                        "qwen2.5-coder-1.5b-q8_0-ctx2048.json")))
+    inventories["qwen2.5-coder-1.5b-q8_0"]["plan_ctx2048"] = {
+        "source": "docs/benchmarks/qwen-2026-10-13/qwen2.5-coder-1.5b-q8_0-ctx2048.json",
+        "context": bench["Context"], "shape": bench["Shape"], "weight_bytes": bench["Plan"]["WeightBytes"],
+        "state_bytes": bench["Plan"]["StateBytes"]}
+
     out = {
         "generated_from": "Satori reference fixtures; regenerate with tests/golden/make_golden.py",
+        "model_inventories": inventories,
         "tolerance_operator": {"abs": 2e-6, "rel": 2e-6, "stated_in": "QwenOperatorTests.cs:24; TransformerOpsTests.cs:16"},
         "gguf_v1": gguf,
         "gguf_v1_files": {"source": "fixtures/gguf/v1/*.gguf and manifest.json", "files": gguf_files},
@@ -97,13 +123,13 @@ def main(ref: str) -> None:
                             "40000000" "00000000" "14000000" "00000000",
         },
     }
-    with open(OUT, "w") as fh:
+    with open(out_path, "w") as fh:
         json.dump(out, fh, separators=(",", ":"))
         fh.write("\n")
-    print(OUT, os.path.getsize(OUT), "bytes")
+    print(out_path, os.path.getsize(out_path), "bytes")
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: python tests/golden/make_golden.py <path to the Satori reference checkout>")
-    main(sys.argv[1])
+    if len(sys.argv) not in (2, 3):
+        sys.exit("usage: python tests/golden/make_golden.py <path to the Satori reference checkout> [output]")
+    main(*sys.argv[1:])
