@@ -20,8 +20,9 @@ here once, as data, together with where each came from:
   tools/attention_reference.py:4-6, restated in tests/golden_util.py.
 * The Ternary2 encoding KAT (Ternary2Tests.cs:9-22) and the STQ2 header KAT
   (MappedTernary2Tests.cs:40-46) are byte strings stated in those tests; they are copied too.
-* ``docs/scouting/inventories/qwen2.5-coder-{1.5b-q8_0,7b-q4_0}.json`` -- the GGUF catalogues of two
-  real models (scalar metadata, every tensor's name / type / dimensions / offset / length) and the plan
+* ``docs/scouting/inventories/{qwen2.5-coder-1.5b-q8_0,qwen2.5-coder-7b-q4_0,qwen2.5-coder-7b-q4_k_m,
+  qwen3-4b-q8_0}.json`` -- the GGUF catalogues of four real models (scalar metadata, every tensor's name /
+  type / dimensions / offset / length) and the plan
   of ``docs/benchmarks/qwen-2026-10-13/qwen2.5-coder-1.5b-q8_0-ctx2048.json`` (shape, weight and KV
   state bytes), for the model-shape and native-loader tests.
 """
@@ -83,7 +84,7 @@ def main(ref: str, out_path: str = OUT) -> None:
     # every tensor's name, type, dimensions, relative offset and length; the arrays' values are not
     # recorded there), and the plan the reference's benchmark reported for the 1.5B model at context 2048.
     inventories = {}
-    for name in ("qwen2.5-coder-1.5b-q8_0", "qwen2.5-coder-7b-q4_0"):
+    for name in ("qwen2.5-coder-1.5b-q8_0", "qwen2.5-coder-7b-q4_0", "qwen2.5-coder-7b-q4_k_m", "qwen3-4b-q8_0"):
         inv = json.load(open(os.path.join(ref, "docs", "scouting", "inventories", name + ".json")))
         meta = [[m["Key"], m["TypeName"], m["Value"]] for m in inv["Metadata"]
                 if m["TypeName"] != "Array" and not m["Key"].startswith("tokenizer.chat")]

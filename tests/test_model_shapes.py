@@ -9,7 +9,8 @@ models (no GPU):
   embedding and the output projection have the same dimensions, in Q8_0 as the benchmark configuration
   states rather than the file's Q4_0 / Q6_K;
 * the native loader (``satori_gguf_open`` + ``satori_gguf_model_desc``) on a sparse container holding each
-  real catalogue: it derives the reference's shape for both models.
+  real catalogue (those two, the 7B Q4_K_M file and the qwen3 4B Q8_0 file): it derives each model's
+  description from the recorded metadata and tensors.
 """
 import struct
 
@@ -84,7 +85,8 @@ def _catalogue_container(tmp_path, inv, name):
         t = types[type_name]
         entries.append(G.entry(key, t, int(value) if t == G.BOOL else value))
     tensors = [(n, dims, t, off) for n, t, dims, off, _ in inv["tensors"]]
-    head = G.prefix(inv["alignment"], b"".join(entries), len(entries), tensors, arch="qwen2")
+    arch = next(value for key, _, value in inv["metadata"] if key == "general.architecture")
+    head = G.prefix(inv["alignment"], b"".join(entries), len(entries), tensors, arch=arch)
     end = max(off + length for _, _, _, off, length in inv["tensors"])
     end = (end + inv["alignment"] - 1) // inv["alignment"] * inv["alignment"]
     path = tmp_path / name
@@ -97,18 +99,39 @@ def _catalogue_container(tmp_path, inv, name):
     return str(path)
 
 
+def _expected_description(inv):
+    """The description DenseTransformerAdapter derives, read off the recorded catalogue: the {arch}.* keys,
+    head length = key_length when declared (else embedding / heads), vocabulary = token_embd's rows, tied
+    when there is no output.weight."""
+    meta = {key: value for key, _, value in inv["metadata"]}
+    arch = meta["general.architecture"]
+    dims = {name: d for name, _, d, _, _ in inv["tensors"]}
+    hidden, heads = meta[f"{arch}.embedding_length"], meta[f"{arch}.attention.head_count"]
+    head_dim = meta.get(f"{arch}.attention.key_length", hidden // heads)
+    return ((meta[f"{arch}.block_count"], hidden, meta[f"{arch}.feed_forward_length"], heads,
+             meta[f"{arch}.attention.head_count_kv"], head_dim, dims["token_embd.weight"][1]),
+            "output.weight" not in dims, arch)
+
+
 @pytest.mark.parametrize("model,expected", [
     ("qwen2.5-coder-1.5b-q8_0", (28, 1536, 8960, 12, 2, 128, 151936)),
     ("qwen2.5-coder-7b-q4_0", (28, 3584, 18944, 28, 4, 128, 152064)),
+    ("qwen2.5-coder-7b-q4_k_m", (28, 3584, 18944, 28, 4, 128, 152064)),
+    ("qwen3-4b-q8_0", None),
 ])
 def test_native_loader_derives_the_real_models_shape(sat, tmp_path, model, expected):
+    """Q8_0, Q4_0 with a Q6_K output, the K-quant mix of Q4_K_M, and qwen3 (per-head q/k norms, a declared
+    key length, tied embeddings): every tensor of each catalogue enters the description."""
     inv = INV[model]
+    want, tied, arch = _expected_description(inv)
+    if expected is not None:
+        assert want == expected
     with sat.GgufFile(_catalogue_container(tmp_path, inv, model + ".gguf")) as g:
         assert len(g.tensors) == inv["tensor_count"]
         d = g.model_desc()
-        assert g.read_scalar("qwen2.rope.freq_base") == pytest.approx(1e6)
-    assert (d["layers"], d["hidden"], d["ffn"], d["q_heads"], d["kv_heads"], d["head_dim"], d["vocab"]) == expected
-    assert not d["tied_embeddings"]                  # both files carry output.weight
-    assert d["tensors"] == 339                       # every required tensor plus the q/k/v biases
-    assert d["rope_base"] == 1e6 and d["rms_epsilon"] == pytest.approx(1e-6)
+        assert g.read_scalar(f"{arch}.rope.freq_base") == pytest.approx(1e6)
+    assert (d["layers"], d["hidden"], d["ffn"], d["q_heads"], d["kv_heads"], d["head_dim"], d["vocab"]) == want
+    assert d["tied_embeddings"] == tied
+    assert d["tensors"] == inv["tensor_count"]
+    assert d["rope_base"] == 1e6
     assert struct.pack("<f", d["rms_epsilon"]) == struct.pack("<f", 1e-6)
