@@ -364,7 +364,8 @@ int map_file(const char *path, int64_t limit, int *fd_out, const uint8_t **map_o
     }
     if ((int64_t)st.st_size > limit) {
         close(fd);
-        return set_error(SATORI_ERR_NOT_SUPPORTED, "File limit: 1 TiB.");
+        if (limit == kFileLimit) return set_error(SATORI_ERR_NOT_SUPPORTED, "File limit: 1 TiB.");
+        return set_error(SATORI_ERR_NOT_SUPPORTED, "File limit: %lld bytes.", (long long)limit);
     }
     *fd_out = fd;
     *len_out = (int64_t)st.st_size;
